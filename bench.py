@@ -1,0 +1,389 @@
+#!/usr/bin/env python
+"""Benchmark: CRT-emulated float64 GEMM on B200 (emulated TFLOP/s = 2mnk / t).
+
+Workload per GPU: C = A @ B with m = n = k = 8192 float64, entries (U(0,1)-0.5)*exp(phi*N(0,1))
+(phi = 1, seeded), the reference's default modulus count (25 primes at k = 8192).  With N GPUs
+the output is a pr x pc grid of 8192 x 8192 blocks (1x1, 1x2, 2x2, 2x4), one per GPU, each
+rank holding its A row panel and B column panel: the product shards with no data-path
+collective, so per-GPU work is fixed ("scaling": "weak").
+
+One JSON line on rank 0:
+  value      device time of K steps (CUDA events, barrier + synchronize on both sides, max
+             over ranks), inputs resident in HBM (2 x 512 MiB per GPU, larger than L2)
+  e2e        the public API crt_matmul() on pinned host tensors: host->device copy of A and B,
+             the product, device->host copy of C, all inside the timed region
+  roofline   the residue GEMM kernel (K2) timed live with CUDA events between stages:
+             achieved int8 tera-ops/s vs the int8 tensor peak
+  cpu_baseline  the CPU oracle (a C restatement of the reference's CPU path) on a sampled
+             sub-block at full k, all host threads, rank 0 at N=1 only
+``--impl reference`` times only that CPU restatement (rank 0; other ranks exit at once).
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "emulated FP64 GEMM TFLOP/s at 8192³, 1/2/4/8 B200; % of int8 TC peak"
+UNIT = "TFLOP/s"
+GRIDS = {1: (1, 1), 2: (1, 2), 4: (2, 2), 8: (2, 4)}
+# dram__bytes_read.sum + dram__bytes_write.sum of one residue-GEMM launch at 8192^3 (25 moduli),
+# from the ncu capture summarised in profiles/residue_gemm_8192.md; None until captured.
+GEMM_DRAM_BYTES_8192 = None
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=100)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--size", type=int, default=8192)
+    p.add_argument("--phi", type=float, default=1.0)
+    p.add_argument("--e2e-steps", type=int, default=10)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def synth(shape, seed, phi, device):
+    import torch
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    u = torch.rand(*shape, generator=g, dtype=torch.float64, device=device) - 0.5
+    return u * torch.exp(phi * torch.randn(*shape, generator=g, dtype=torch.float64,
+                                           device=device))
+
+
+# ---------------------------------------------------------------------------------------
+# CPU baseline: the oracle on a sampled s x k by k x s sub-block
+# ---------------------------------------------------------------------------------------
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_sample_run(k, s, phi, seed=7):
+    import torch
+
+    from oracle import oracle
+
+    A = synth((s, k), seed, phi, "cpu").numpy()
+    B = synth((k, s), seed + 1, phi, "cpu").numpy()
+    t0 = time.perf_counter()
+    oracle.crt_matmul(A, B, 53)
+    t = time.perf_counter() - t0
+    del torch
+    return t
+
+
+def calibrate_cpu_sample(k, phi, target_s=4.0):
+    """Largest power-of-two sample edge s (64..2048) whose oracle run stays near target_s."""
+    s = 64
+    t = cpu_sample_run(k, s, phi)
+    while s < 2048 and t * 4.5 < target_s:  # one doubling costs about 2x-4x
+        s *= 2
+        t = cpu_sample_run(k, s, phi)
+    return s
+
+
+def cpu_baseline(k, phi, target_s=4.0, reps=2):
+    s = calibrate_cpu_sample(k, phi, target_s)
+    best = min(cpu_sample_run(k, s, phi) for _ in range(reps))
+    return {
+        "value": 2.0 * s * s * k / best / 1e12,
+        "unit": UNIT,
+        "cores": cpu_threads(),
+        "kind": "port",
+        "sample": f"{s}x{k} @ {k}x{s} sub-block of the {k}^3 workload (rows of A, columns of B "
+                  f"at full k), C oracle (split + int32 residue GEMM + bigint CRT), OpenMP, "
+                  f"best of {reps}, {best:.2f} s per run",
+    }
+
+
+# ---------------------------------------------------------------------------------------
+# GPU helpers
+# ---------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.proc = None
+        self.lines = []
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(gpu_index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r.split(",") for r in out.strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows]
+        smax = max(float(r[2]) for r in rows)
+        loaded = [r for r in rows if float(r[3]) > 200.0] or rows
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in loaded:
+            for name, val in zip(names, r[5:9]):
+                if val.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(float(r[1]) for r in loaded), "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(rows), "samples_under_load": len(loaded),
+                "sm_mhz_min": min(sm)}
+
+
+def measure_int8_peak(torch, dev, size=8192, reps=10):
+    """cuBLAS int8 GEMM (torch._int_mm) burst throughput in tera-ops/s."""
+    a = torch.randint(-64, 64, (size, size), dtype=torch.int8, device=dev)
+    b = torch.randint(-64, 64, (size, size), dtype=torch.int8, device=dev)
+    for _ in range(3):
+        torch._int_mm(a, b)
+    best = float("inf")
+    for _ in range(reps):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        torch._int_mm(a, b)
+        e.record()
+        e.synchronize()
+        best = min(best, s.elapsed_time(e))
+    del a, b
+    return 2.0 * size**3 / (best * 1e-3) / 1e12
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    k = args.size
+    # size each step so that warm-up + timed steps stay within about 150 s
+    target = max(0.2, min(4.0, 150.0 / max(1, args.steps + args.warmup)))
+    s = calibrate_cpu_sample(k, args.phi, target_s=target)
+    for _ in range(args.warmup):
+        cpu_sample_run(k, s, args.phi)
+    times = [cpu_sample_run(k, s, args.phi) for _ in range(args.steps)]
+    t = statistics.mean(times)
+    value = 2.0 * s * s * k / t / 1e12
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "i8",
+        "data": f"synthetic (U(0,1)-0.5)*exp({args.phi}*N(0,1)), seeded, generated on the host",
+        "config": {"workload": f"CRT-emulated DGEMM {k}^3 FP64, sampled {s}x{k} @ {k}x{s} "
+                               "sub-block per step on the host CPU",
+                   "m": s, "n": s, "k": k, "n_moduli": 25},
+        "impl": "reference",
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+                         "sample": f"{s}x{k} @ {k}x{s} per step, C restatement of the "
+                                   "reference CPU path (oracle/), OpenMP over all host threads"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import torch
+
+    import tensor_inv_b200 as ti
+    from tensor_inv_b200 import _native as nat
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=180))
+    pr, pc = GRIDS.get(world, (1, world))
+    br, bc = rank // pc, rank % pc
+    m = n = k = args.size
+    bits = 53
+    n_mod = nat.n_moduli(k, bits)
+
+    A = synth((m, k), 1000 + br, args.phi, dev)
+    B = synth((k, n), 2000 + bc, args.phi, dev)
+    C = torch.empty((m, n), dtype=torch.float64, device=dev)
+    ws_bytes = nat.crt_workspace_size(m, n, k, bits)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    L = nat.lib()
+
+    def step(events=None):
+        ev = None
+        if events is not None:
+            ev = (ctypes.c_void_p * 4)(*[e.cuda_event for e in events])
+        st = L.ti_crt_matmul_events(A.data_ptr(), k, 1, B.data_ptr(), n, 1, C.data_ptr(), n, m,
+                                    n, k, bits, 0, ws.data_ptr(), ws_bytes, stream.cuda_stream,
+                                    ev)
+        nat.check("ti_crt_matmul", st)
+
+    def barrier():
+        torch.cuda.synchronize(dev)
+        if dist is not None:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- warm-up
+    for _ in range(args.warmup):
+        step()
+    barrier()
+
+    # ---- timed region: K steps, inputs resident (larger than L2)
+    stage_events = []
+    for _ in range(args.steps):
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        for e in evs:
+            e.record(stream)  # materialise the event handles
+        stage_events.append(evs)
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(local) if rank == 0 else None
+    time.sleep(0.3 if sampler else 0.0)
+    barrier()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for i in range(args.steps):
+        step(stage_events[i])
+    t_end.record(stream)
+    barrier()
+    clocks = sampler.stop() if sampler else None
+    ms = t_start.elapsed_time(t_end) / args.steps
+    ms = max_over_ranks(ms)
+    k1 = statistics.mean(e[0].elapsed_time(e[1]) for e in stage_events)
+    k2 = statistics.mean(e[1].elapsed_time(e[2]) for e in stage_events)
+    k3 = statistics.mean(e[2].elapsed_time(e[3]) for e in stage_events)
+    flops = 2.0 * m * n * k
+    value = world * flops / (ms * 1e-3) / 1e12
+
+    # ---- correctness spot check of this rank's block against the CPU oracle (untimed)
+    spot_ok = None
+    if rank == 0:
+        from oracle import oracle
+
+        r0, c0 = 4000, 5000
+        want = oracle.crt_matmul(A[r0:r0 + 16].cpu().numpy(), B[:, c0:c0 + 16].cpu().numpy(), 53)
+        got = C[r0:r0 + 16, c0:c0 + 16].cpu().numpy()
+        spot_ok = bool((got.view("u8") == want.view("u8")).all())
+
+    # ---- e2e: public API on pinned host tensors, copies inside the timed region
+    Ah = A.cpu().pin_memory()
+    Bh = B.cpu().pin_memory()
+    for _ in range(2):
+        ti.crt_matmul(Ah, Bh)
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    w0 = time.perf_counter()
+    e0.record(stream)
+    for _ in range(args.e2e_steps):
+        Ch = ti.crt_matmul(Ah, Bh)
+    e1.record(stream)
+    barrier()
+    wall_e2e = (time.perf_counter() - w0) / args.e2e_steps
+    ms_e2e = max_over_ranks(e0.elapsed_time(e1) / args.e2e_steps)
+    assert Ch.device.type == "cpu" and Ch.shape == (m, n)
+    e2e = {"value": world * flops / (ms_e2e * 1e-3) / 1e12, "unit": UNIT,
+           "h2d_bytes_per_step": Ah.numel() * 8 + Bh.numel() * 8,
+           "d2h_bytes_per_step": Ch.numel() * 8, "ms_per_step": ms_e2e,
+           "wall_ms_per_step": wall_e2e * 1e3}
+    del Ah, Bh, Ch
+
+    # ---- int8 tensor peak (cuBLAS int8 burst, and 2x the measured bf16 dense peak)
+    peaks_file = ROOT / "MEASURED_PEAKS.json"
+    bf16 = None
+    if peaks_file.exists():
+        bf16 = json.loads(peaks_file.read_text()).get("bf16_tflops")
+    int8_cublas = measure_int8_peak(torch, dev) if rank == 0 else None
+    cands = [x for x in (int8_cublas, 2 * bf16 if bf16 else None) if x]
+    peak = max(cands) if cands else 4500.0
+    peak_src = ("max(cuBLAS int8 8192^3 burst measured in this run = "
+                f"{int8_cublas:.0f}, 2 x measured bf16 dense {bf16} = "
+                f"{2 * bf16 if bf16 else float('nan'):.0f}) tera-ops/s" if cands else
+                "fallback: datasheet 4500 dense int8 tera-ops/s")
+    gemm_ops = 2.0 * m * n * k * n_mod
+    achieved = gemm_ops / (k2 * 1e-3) / 1e12
+    roof = {"bound": "tensor", "kernel": "residue_gemm_kernel (K2, tcgen05 kind::i8)",
+            "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+            "traffic": GEMM_DRAM_BYTES_8192 if (m, n, k) == (8192, 8192, 8192) else None,
+            "peak_source": peak_src + " (of measured)",
+            "ops_per_launch": gemm_ops, "ms_per_launch": k2,
+            "note": "int8 ops: 2*m*n*k per modulus x 25 moduli; unit is tera int8-ops/s"}
+    bytes_k1 = (8 * 2 + n_mod) * (m * k + k * n)  # two float64 reads (exp + split) + residues
+    bytes_k3 = n_mod * m * n + 8 * m * n
+    stages = {"k1_split_ms": k1, "k1_gbs": bytes_k1 / (k1 * 1e-3) / 1e9,
+              "k2_gemm_ms": k2, "k3_crt_ms": k3, "k3_gbs": bytes_k3 / (k3 * 1e-3) / 1e9,
+              "emulated_tflops_ceiling_at_peak": peak / n_mod}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(k, args.phi)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "i8",
+            "data": f"synthetic (U(0,1)-0.5)*exp({args.phi}*N(0,1)), seeded per panel, "
+                    "generated on the device",
+            "config": {"workload": f"CRT-emulated DGEMM m=n=k={m} FP64 per GPU, default "
+                                   f"{n_mod} moduli, output grid {pr}x{pc} of {m}x{n} blocks",
+                       "m": m, "n": n, "k": k, "n_moduli": n_mod, "grid": f"{pr}x{pc}",
+                       "l2": "inputs larger than L2 (2 x 512 MiB float64 per GPU)",
+                       "parallelism": f"output blocks over {world} GPU(s), no collective"},
+            "e2e": e2e, "roofline": roof, "cpu_baseline": cpu, "clocks": clocks,
+            "gpu_launches": 6 * args.steps, "stages": stages, "spot_check_bitexact": spot_ok,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

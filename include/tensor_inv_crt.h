@@ -1,0 +1,148 @@
+/*
+ * tensor_inv_crt.h -- C ABI of libtensor_inv_crt.so, the B200 (sm_100a) implementation
+ * of tensor_inv's CRT-emulated float64 matmul ("Ozaki scheme II" with the first N odd
+ * primes as moduli).
+ *
+ * Conventions
+ *   - Every pointer marked "device" is CUDA device memory on the current device.
+ *   - Every call is asynchronous on `stream` (a cudaStream_t passed as void*; NULL is the
+ *     legacy default stream) and returns a ti_status_t.  Nothing allocates device memory:
+ *     calls that need scratch space take a caller-owned workspace.
+ *   - Matrices are described by element strides: element (i, j) of an m x n matrix X
+ *     lives at X[i*s0 + j*s1].  One of the two strides must be 1.
+ *   - bits is the number of significand bits kept per input element (the reference's
+ *     _PRECISION_BITS: 53 float64, 24 float32, 11 float16, 8 bfloat16).
+ *
+ * Reference interfaces replaced (paths inside the reference project):
+ *   ti_n_moduli               src/tensor_inv/crt_matmul.py:26      _n_moduli(k, bits)
+ *   ti_crt_split              src/tensor_inv/crt_matmul.py:38,47   _scale_to_int + _residues
+ *   ti_batched_int8_gemm_mod  src/tensor_inv/csrc/crt_kernel.cu:17 batched_int8_gemm_mod
+ *   ti_crt_reconstruct        src/tensor_inv/csrc/crt_kernel.cu:127 crt_reconstruct
+ *   ti_crt_matmul             src/tensor_inv/crt_matmul.py:101     crt_matmul (CUDA branch)
+ */
+#ifndef TENSOR_INV_CRT_H
+#define TENSOR_INV_CRT_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    TI_OK = 0,
+    TI_ERR_INVALID_ARGUMENT = 1, /* bad shape, stride, dtype bits or null pointer */
+    TI_ERR_UNSUPPORTED = 2,      /* k beyond the int32 accumulator bound or the moduli set */
+    TI_ERR_WORKSPACE = 3,        /* workspace too small or misaligned */
+    TI_ERR_CUDA = 4,             /* a CUDA runtime/driver call failed */
+    TI_ERR_DEVICE_TIMEOUT = 5,   /* a kernel gave up on a bounded wait (see ti_device_error) */
+    TI_ERR_NO_DEVICE = 6         /* no sm_100 device, or the driver entry point is missing */
+} ti_status_t;
+
+/* Row/column exponent value that marks a row of A (or column of B) holding a NaN or an
+   infinity; the matching output row (column) is NaN. */
+#define TI_NONFINITE_EXP (-2147483647 - 1)
+
+/* Largest inner dimension: 126*126*k must stay below 2^31 in the int32 accumulators. */
+#define TI_MAX_K 135263
+
+/* Human-readable name of a status code (static string). */
+const char *ti_status_string(int status);
+
+/* Library version, e.g. "0.1.0". */
+const char *ti_version(void);
+
+/* Replaces crt_matmul.py:26 _n_moduli: smallest N with prod(first N odd primes) >
+   2*k*2^(2*bits).  Writes N to *n_out; TI_ERR_UNSUPPORTED if no N <= 30 works. */
+int ti_n_moduli(int64_t k, int bits, int *n_out);
+
+/* The 30 moduli (3, 5, 7, ..., 127), in order. */
+const int32_t *ti_primes(void);
+
+/* Workspace bytes ti_crt_matmul needs for an m x k by k x n product at `bits`. */
+int ti_crt_workspace_size(int64_t m, int64_t n, int64_t k, int bits, size_t *bytes);
+
+/*
+ * Replaces crt_matmul.py:38 _scale_to_int + crt_matmul.py:47 _residues for one operand.
+ * The operand is `outer` vectors of length `kdim` (rows of A, or columns of B); element
+ * (o, l) is X[o*s_outer + l*s_k] (device, float64).
+ *   exp_out[o]   (device int32[outer]) = frexp(max(max_l |x|, 1e-300)).exponent,
+ *                or TI_NONFINITE_EXP
+ *   res_out      (device int8, [n_mod][outer][ld_res]) = nearbyint(x * 2^(bits-exp)) mod p_i,
+ *                in [0, p_i); columns kdim..ld_res-1 are written as 0.
+ * ld_res must be a multiple of 16 and >= kdim; res_out must be 16-byte aligned.
+ */
+int ti_crt_split(const double *X, int64_t outer, int64_t kdim, int64_t s_outer, int64_t s_k,
+                 int bits, int n_mod, int32_t *exp_out, int8_t *res_out, int64_t ld_res,
+                 void *stream);
+
+/*
+ * Replaces crt_kernel.cu:17 batched_int8_gemm_mod (cuBLASLt int8 GEMM + mod_reduce):
+ *   c[i] = (a[i] @ b[i]) mod moduli[i], with the result in [0, moduli[i]).
+ * a: device int8 (batch, M, K) row-major; b: device int8 (batch, K, N) row-major;
+ * c: device int32 (batch, M, N) row-major; moduli: HOST int32[batch], each in [2, 256).
+ * Unlike the reference, M, K and N need no padding.  Runs on tcgen05 tensor cores.
+ * workspace: device scratch of ti_batched_gemm_workspace_size() bytes, 256-byte aligned.
+ */
+int ti_batched_gemm_workspace_size(int64_t batch, int64_t M, int64_t K, int64_t N,
+                                   size_t *bytes);
+int ti_batched_int8_gemm_mod(const int8_t *a, const int8_t *b, const int32_t *moduli,
+                             int64_t batch, int64_t M, int64_t K, int64_t N, int32_t *c,
+                             void *workspace, size_t workspace_bytes, void *stream);
+
+/*
+ * Replaces crt_kernel.cu:127 crt_reconstruct.  Exact integer CRT (not the reference GPU
+ * kernel's double-double approximation): x = sum_i r_i M_i (M_i^-1 mod p_i) mod M, lifted
+ * to (-M/2, M/2], then out = ldexp((double)x, row_exp[r] + col_exp[c] - 2*bits) with the
+ * rounding of Python's float(int) followed by math.ldexp.  Bit-identical to the
+ * reference's CPU path (crt_matmul.py:79-98).
+ * residues: device int32 (n_mod, rows, cols); moduli: HOST int32[n_mod], pairwise coprime,
+ * each in [2, 256), product below 2^127; row_exp/col_exp: device int32; out: device
+ * float64 rows x cols with leading dimension ldo.
+ */
+int ti_crt_reconstruct(const int32_t *residues, const int32_t *moduli, int n_mod, int bits,
+                       const int32_t *row_exp, const int32_t *col_exp, int64_t rows,
+                       int64_t cols, double *out, int64_t ldo, void *stream);
+
+/* Output modes of ti_crt_matmul. */
+#define TI_OUT_STORE 0    /* C  = A @ B  */
+#define TI_OUT_SUBTRACT 1 /* C -= A @ B  (C - round(A@B), as `W -= crt_matmul(...)`) */
+#define TI_OUT_ADD 2      /* C += A @ B  */
+
+/*
+ * Replaces crt_matmul.py:101 crt_matmul for float64 operands on the device:
+ *   A (m x k): element (i, l) at A[i*sa0 + l*sa1];  B (k x n): (l, j) at B[l*sb0 + j*sb1];
+ *   C (m x n) row-major with leading dimension ldc.
+ * Output bits equal the reference CPU path for finite inputs.  Stages: split A and B into
+ * int8 residues (K1), one tcgen05 int8 GEMM per modulus with the mod-reduce in its
+ * epilogue (K2), exact CRT reconstruction + inverse scaling (K3).
+ * workspace: device scratch of ti_crt_workspace_size() bytes, 256-byte aligned.
+ */
+int ti_crt_matmul(const double *A, int64_t sa0, int64_t sa1, const double *B, int64_t sb0,
+                  int64_t sb1, double *C, int64_t ldc, int64_t m, int64_t n, int64_t k,
+                  int bits, int out_mode, void *workspace, size_t workspace_bytes,
+                  void *stream);
+
+/*
+ * ti_crt_matmul that also records four caller-created CUDA events (cudaEvent_t, passed as
+ * void*; NULL entries are skipped) on `stream`: stage_events[0] before K1 (split),
+ * [1] before K2 (residue GEMM), [2] before K3 (CRT), [3] after K3.  For profiling; the
+ * events add no synchronisation.
+ */
+int ti_crt_matmul_events(const double *A, int64_t sa0, int64_t sa1, const double *B,
+                         int64_t sb0, int64_t sb1, double *C, int64_t ldc, int64_t m, int64_t n,
+                         int64_t k, int bits, int out_mode, void *workspace,
+                         size_t workspace_bytes, void *stream, void *const *stage_events);
+
+/*
+ * Reads (and, if reset != 0, clears) the current device's kernel error word.  Kernels set
+ * it instead of hanging when a bounded wait runs out; 0 means no error.  Synchronous.
+ */
+int ti_device_error(int *code_out, int reset);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TENSOR_INV_CRT_H */

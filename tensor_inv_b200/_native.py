@@ -1,0 +1,115 @@
+"""ctypes binding of ``libtensor_inv_crt.so`` (the C ABI in ``include/tensor_inv_crt.h``).
+
+The library is the only compute path: there is no CPU or PyTorch fallback.  Loading it
+needs no GPU (so the CPU test suite can check its exports); every compute entry point
+returns ``TI_ERR_NO_DEVICE`` unless an sm_100 device is current.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libtensor_inv_crt.so"
+
+TI_OK = 0
+TI_ERR_INVALID_ARGUMENT = 1
+TI_ERR_UNSUPPORTED = 2
+TI_ERR_WORKSPACE = 3
+TI_ERR_CUDA = 4
+TI_ERR_DEVICE_TIMEOUT = 5
+TI_ERR_NO_DEVICE = 6
+
+TI_OUT_STORE = 0
+TI_OUT_SUBTRACT = 1
+TI_OUT_ADD = 2
+
+TI_NONFINITE_EXP = -(2**31)
+TI_MAX_K = 135263
+
+# name -> (restype, argtypes); mirrors include/tensor_inv_crt.h
+_i64, _int, _p, _sz = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t
+SIGNATURES = {
+    "ti_status_string": (ctypes.c_char_p, [_int]),
+    "ti_version": (ctypes.c_char_p, []),
+    "ti_n_moduli": (_int, [_i64, _int, ctypes.POINTER(_int)]),
+    "ti_primes": (ctypes.POINTER(ctypes.c_int32), []),
+    "ti_crt_workspace_size": (_int, [_i64, _i64, _i64, _int, ctypes.POINTER(_sz)]),
+    "ti_crt_split": (_int, [_p, _i64, _i64, _i64, _i64, _int, _int, _p, _p, _i64, _p]),
+    "ti_batched_gemm_workspace_size": (_int, [_i64, _i64, _i64, _i64, ctypes.POINTER(_sz)]),
+    "ti_batched_int8_gemm_mod": (_int, [_p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _sz, _p]),
+    "ti_crt_reconstruct": (_int, [_p, _p, _int, _int, _p, _p, _i64, _i64, _p, _i64, _p]),
+    "ti_crt_matmul": (_int, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i64, _i64, _int,
+                             _int, _p, _sz, _p]),
+    "ti_crt_matmul_events": (_int, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i64, _i64,
+                                    _int, _int, _p, _sz, _p, _p]),
+    "ti_device_error": (_int, [ctypes.POINTER(_int), _int]),
+}
+
+_lib = None
+
+
+class NativeError(RuntimeError):
+    """A non-zero ti_status_t from the library."""
+
+    def __init__(self, fn: str, status: int):
+        self.status = status
+        super().__init__(f"{fn} failed: {status_string(status)} (status {status})")
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                f"{LIB_PATH.name} is not built; run `python -m tensor_inv_b200._build` "
+                "(nvcc for sm_100a). tensor_inv_b200 has no CPU fallback.")
+        L = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def status_string(status: int) -> str:
+    return lib().ti_status_string(int(status)).decode()
+
+
+def check(fn: str, status: int) -> None:
+    if status != TI_OK:
+        raise NativeError(fn, status)
+
+
+def n_moduli(k: int, bits: int) -> int:
+    out = ctypes.c_int(0)
+    st = lib().ti_n_moduli(int(k), int(bits), ctypes.byref(out))
+    if st == TI_ERR_UNSUPPORTED:
+        raise ValueError(f"not enough primes for inner dim {k}, bits {bits}")
+    check("ti_n_moduli", st)
+    return out.value
+
+
+def primes() -> list[int]:
+    p = lib().ti_primes()
+    return [int(p[i]) for i in range(30)]
+
+
+def crt_workspace_size(m: int, n: int, k: int, bits: int) -> int:
+    out = ctypes.c_size_t(0)
+    check("ti_crt_workspace_size", lib().ti_crt_workspace_size(m, n, k, bits, ctypes.byref(out)))
+    return out.value
+
+
+def batched_gemm_workspace_size(batch: int, M: int, K: int, N: int) -> int:
+    out = ctypes.c_size_t(0)
+    check("ti_batched_gemm_workspace_size",
+          lib().ti_batched_gemm_workspace_size(batch, M, K, N, ctypes.byref(out)))
+    return out.value
+
+
+def device_error(reset: bool = True) -> int:
+    out = ctypes.c_int(0)
+    check("ti_device_error", lib().ti_device_error(ctypes.byref(out), 1 if reset else 0))
+    return out.value

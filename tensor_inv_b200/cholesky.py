@@ -1,0 +1,46 @@
+"""Blocked right-looking Cholesky; trailing update through the CRT kernels.
+
+Same algorithm and arithmetic as the reference (src/tensor_inv/cholesky.py:6-35).  The
+trailing update ``W[jb:, jb:] -= crt_matmul(L21, L21.T)`` runs fused on CUDA
+(``crt_matmul_update``) with ``L21.T`` consumed as a transposed view (no copy).
+"""
+
+import torch
+
+from tensor_inv_b200.crt_matmul import crt_matmul, crt_matmul_update
+
+
+def cholesky(A, block_size=64):
+    """
+    Blocked Cholesky: panel via torch, trailing GEMM via CRT int8.
+
+    A must be symmetric positive definite.
+    """
+    if A.shape[0] != A.shape[1]:
+        raise ValueError(f"expected square matrix, got {A.shape}")
+
+    n = A.shape[0]
+    L = torch.zeros_like(A)
+    W = A.clone()
+
+    for j in range(0, n, block_size):
+        b = min(block_size, n - j)
+        jb = j + b
+
+        # panel: small Cholesky on the diagonal block (cholesky.py:24)
+        L[j:jb, j:jb] = torch.linalg.cholesky(W[j:jb, j:jb])
+
+        if jb < n:
+            # panel: triangular solve for the sub-diagonal block (cholesky.py:28-30)
+            L[jb:, j:jb] = torch.linalg.solve_triangular(
+                L[j:jb, j:jb], W[jb:, j:jb].T, upper=False
+            ).T
+
+            # trailing GEMM update via CRT (cholesky.py:33)
+            L21 = L[jb:, j:jb]
+            if W.is_cuda and W.dtype == torch.float64:
+                crt_matmul_update(W[jb:, jb:], L21, L21.T, alpha=-1)
+            else:
+                W[jb:, jb:] -= crt_matmul(L21, L21.T)
+
+    return L

@@ -1,0 +1,439 @@
+// ti_api.cu -- the extern "C" entry points of libtensor_inv_crt.so (include/tensor_inv_crt.h).
+//
+// Host-side planning for the CRT matmul: the modulus count (crt_matmul.py:26 _n_moduli),
+// the per-modulus constants every kernel receives by value, the workspace layout, and the
+// stage sequence K1 (split) -> K2 (tcgen05 residue GEMM) -> K3 (exact CRT).
+#include <cstring>
+
+#include "../../include/tensor_inv_crt.h"
+#include "ti_common.cuh"
+
+namespace ti {
+cudaError_t launch_split(const double *X, int64_t outer, int64_t kdim, int64_t s_outer,
+                         int64_t s_k, const SplitConst &C, int32_t *exp_out, int8_t *res,
+                         int64_t ld_res, int num_sms, cudaStream_t stream);
+cudaError_t launch_residue_gemm(const int8_t *a_res, const int8_t *b_res, int64_t m, int64_t n,
+                                int64_t kdim, int64_t ld, int n_mod, const ModMagic &mm,
+                                void *out, int64_t ldo, int out_i32, int *err, int num_sms,
+                                cudaStream_t stream);
+cudaError_t launch_crt(const void *R, bool in_u8, int64_t ldr, int64_t plane, int64_t rows,
+                       int64_t cols, const int32_t *row_exp, const int32_t *col_exp, double *C,
+                       int64_t ldc, int out_mode, const CrtConst &K, int num_sms,
+                       cudaStream_t stream);
+
+// The device error word: kernels record a bounded wait that ran out here.
+__device__ int g_device_error = 0;
+
+static const int32_t kPrimes[30] = {3,  5,  7,  11, 13, 17, 19, 23, 29,  31,  37,  41,  43,  47,  53,
+                                    59, 61, 67, 71, 73, 79, 83, 89, 97, 101, 103, 107, 109, 113, 127};
+
+typedef unsigned __int128 u128;
+
+static inline int64_t round_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
+static inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// ---------------------------------------------------------------------------------------
+// modulus count: exact comparison of prod(p) with 2*k*2^(2*bits) on 32-bit words
+// ---------------------------------------------------------------------------------------
+static int n_moduli_exact(int64_t k, int bits) {
+    if (k < 0 || bits < 1 || bits > 64) return -1;
+    uint32_t target[10] = {0}, prod[10] = {0};
+    // target = k << (2*bits + 1)
+    const int sh = 2 * bits + 1;
+    u128 kk = static_cast<u128>(static_cast<uint64_t>(k));
+    for (int w = 0; w < 10; ++w) {
+        // bit range [32w, 32w+32) of kk << sh
+        const int lo = 32 * w - sh;
+        uint32_t word = 0;
+        for (int b = 0; b < 32; ++b) {
+            const int src = lo + b;
+            if (src >= 0 && src < 128 && ((kk >> src) & 1)) word |= 1u << b;
+        }
+        target[w] = word;
+    }
+    prod[0] = 1;
+    for (int i = 0; i < 30; ++i) {
+        uint64_t carry = 0;
+        for (int w = 0; w < 10; ++w) {
+            const uint64_t t = static_cast<uint64_t>(prod[w]) * kPrimes[i] + carry;
+            prod[w] = static_cast<uint32_t>(t);
+            carry = t >> 32;
+        }
+        int cmp = 0;
+        for (int w = 9; w >= 0 && cmp == 0; --w)
+            if (prod[w] != target[w]) cmp = prod[w] > target[w] ? 1 : -1;
+        if (cmp > 0) return i + 1;
+    }
+    return -1;
+}
+
+// ---------------------------------------------------------------------------------------
+// per-modulus constants
+// ---------------------------------------------------------------------------------------
+static bool is_pow2(uint32_t x) { return (x & (x - 1)) == 0; }
+
+static bool make_magic(const int32_t *moduli, int n, ModMagic &mm) {
+    if (n < 1 || n > kMaxModuli) return false;
+    std::memset(&mm, 0, sizeof(mm));
+    for (int i = 0; i < n; ++i) {
+        const uint32_t p = static_cast<uint32_t>(moduli[i]);
+        if (moduli[i] < 2 || p >= 256) return false;
+        uint32_t sh = 0;
+        while ((2u << sh) <= p) ++sh;  // floor(log2 p)
+        mm.p[i] = p;
+        mm.shift[i] = sh;
+        // ceil(2^(32+sh) / p) < 2^32 for p not a power of two; powers of two use
+        // magic = 2^32 / p * 2^sh exactly -- not needed by the int8 paths, kept valid anyway
+        const u128 num = static_cast<u128>(1) << (32 + sh);
+        u128 mg = (num + p - 1) / p;
+        if (is_pow2(p)) mg = (static_cast<u128>(1) << 32) - 1;  // unused (uint8 path is odd p)
+        mm.magic[i] = static_cast<uint32_t>(mg);
+    }
+    return true;
+}
+
+static bool make_split_const(int n_mod, int bits, SplitConst &C) {
+    std::memset(&C, 0, sizeof(C));
+    C.n_mod = n_mod;
+    C.bits = bits;
+    if (!make_magic(kPrimes, n_mod, C.mm)) return false;
+    for (int i = 0; i < n_mod; ++i) {
+        const uint64_t p = kPrimes[i];
+        C.w32[i] = static_cast<uint32_t>((uint64_t(1) << 32) % p);
+        C.w16[i] = static_cast<uint32_t>((uint64_t(1) << 16) % p);
+        C.bigp[i] = static_cast<uint32_t>(p * (((uint64_t(1) << 29) + p - 1) / p));
+    }
+    return true;
+}
+
+// Pairwise-coprime moduli with product below 2^127 (so every lifted value fits 128 bits).
+static bool make_crt_const(const int32_t *moduli, int n_mod, int bits, CrtConst &K) {
+    std::memset(&K, 0, sizeof(K));
+    if (!make_magic(moduli, n_mod, K.mm)) return false;
+    K.n_mod = n_mod;
+    K.two_bits = 2 * bits;
+    u128 M = 1;
+    for (int i = 0; i < n_mod; ++i) {
+        const u128 p = static_cast<uint32_t>(moduli[i]);
+        if (M > (static_cast<u128>(1) << 127) / p) return false;
+        M *= p;
+    }
+    if (M >= (static_cast<u128>(1) << 127)) return false;
+    for (int i = 0; i < n_mod; ++i) {
+        const uint32_t p = static_cast<uint32_t>(moduli[i]);
+        const u128 Mi = M / p;
+        const uint32_t red = static_cast<uint32_t>(Mi % p);
+        uint32_t inv = 0;
+        for (uint32_t t = 1; t < p; ++t)
+            if ((static_cast<uint64_t>(red) * t) % p == 1) {
+                inv = t;
+                break;
+            }
+        if (!inv) return false;  // not coprime
+        K.u[i] = inv;
+        K.finv[i] = static_cast<uint32_t>(((uint64_t(1) << 32) + p / 2) / p);
+        for (int w = 0; w < 4; ++w) K.Mi[i][w] = static_cast<uint32_t>(Mi >> (32 * w));
+    }
+    const u128 H = (M - 1) / 2;
+    for (int w = 0; w < 4; ++w) {
+        K.M[w] = static_cast<uint32_t>(M >> (32 * w));
+        K.H[w] = static_cast<uint32_t>(H >> (32 * w));
+    }
+    return true;
+}
+
+// ---------------------------------------------------------------------------------------
+// device bookkeeping
+// ---------------------------------------------------------------------------------------
+struct DevInfo {
+    int num_sms;
+    int *err;
+};
+
+static int device_info(DevInfo &d) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return TI_ERR_NO_DEVICE;
+    int major = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+        return TI_ERR_NO_DEVICE;
+    if (major != 10) return TI_ERR_NO_DEVICE;
+    if (cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return TI_ERR_CUDA;
+    if (cudaGetSymbolAddress(reinterpret_cast<void **>(&d.err), g_device_error) != cudaSuccess)
+        return TI_ERR_CUDA;
+    return TI_OK;
+}
+
+static int cuda_status(cudaError_t e) { return e == cudaSuccess ? TI_OK : TI_ERR_CUDA; }
+
+// ---------------------------------------------------------------------------------------
+// int8 repacking for the reference-layout batched GEMM entry point
+// ---------------------------------------------------------------------------------------
+// dst[b][r][0..ld) = src[b][r][0..K) followed by zeros
+__global__ void pad_rows_i8_kernel(const int8_t *__restrict__ src, int64_t batch, int64_t rows,
+                                   int64_t K, int8_t *__restrict__ dst, int64_t ld) {
+    const int64_t total = batch * rows * ld;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t br = i / ld, c = i - br * ld;
+        dst[i] = c < K ? src[br * K + c] : 0;
+    }
+}
+
+// dst[b][n][0..ld) = src[b][0..K)[n] followed by zeros (transpose of each K x N plane)
+__global__ void transpose_i8_kernel(const int8_t *__restrict__ src, int64_t batch, int64_t K,
+                                    int64_t N, int8_t *__restrict__ dst, int64_t ld) {
+    __shared__ int8_t tile[64][65];
+    const int64_t tk = (ld + 63) / 64, tn = (N + 63) / 64;
+    for (int64_t t = blockIdx.x; t < batch * tk * tn; t += gridDim.x) {
+        const int64_t b = t / (tk * tn), r = t - b * tk * tn;
+        const int64_t k0 = (r / tn) * 64, n0 = (r % tn) * 64;
+        for (int i = threadIdx.x; i < 64 * 64; i += blockDim.x) {
+            const int kk = i / 64, nn = i % 64;
+            const int64_t k = k0 + kk, n = n0 + nn;
+            tile[kk][nn] = (k < K && n < N) ? src[(b * K + k) * N + n] : 0;
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < 64 * 64; i += blockDim.x) {
+            const int nn = i / 64, kk = i % 64;
+            const int64_t k = k0 + kk, n = n0 + nn;
+            if (n < N && k < ld) dst[(b * N + n) * ld + k] = tile[kk][nn];
+        }
+        __syncthreads();
+    }
+}
+
+}  // namespace ti
+
+using namespace ti;
+
+// =======================================================================================
+// C ABI
+// =======================================================================================
+extern "C" {
+
+const char *ti_status_string(int status) {
+    switch (status) {
+        case TI_OK: return "ok";
+        case TI_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case TI_ERR_UNSUPPORTED: return "unsupported size (inner dimension or moduli)";
+        case TI_ERR_WORKSPACE: return "workspace too small or misaligned";
+        case TI_ERR_CUDA: return "CUDA error";
+        case TI_ERR_DEVICE_TIMEOUT: return "device wait timed out";
+        case TI_ERR_NO_DEVICE: return "no sm_100 device";
+        default: return "unknown status";
+    }
+}
+
+const char *ti_version(void) { return "0.1.0"; }
+
+const int32_t *ti_primes(void) { return kPrimes; }
+
+int ti_n_moduli(int64_t k, int bits, int *n_out) {
+    if (!n_out) return TI_ERR_INVALID_ARGUMENT;
+    const int n = n_moduli_exact(k, bits);
+    if (n < 0) return TI_ERR_UNSUPPORTED;
+    *n_out = n;
+    return TI_OK;
+}
+
+// Workspace layout of ti_crt_matmul (each piece 256-byte aligned):
+//   row_exp int32[m] | col_exp int32[n] | A residues int8[N][m][ldk] |
+//   B residues int8[N][n][ldk] | product residues uint8[N][m][ldr]
+struct CrtLayout {
+    int n_mod;
+    int64_t ldk, ldr;
+    size_t off_rexp, off_cexp, off_a, off_b, off_r, total;
+};
+
+static int crt_layout(int64_t m, int64_t n, int64_t k, int bits, CrtLayout &L) {
+    if (m < 0 || n < 0 || k < 0) return TI_ERR_INVALID_ARGUMENT;
+    if (bits != 8 && bits != 11 && bits != 24 && bits != 53) return TI_ERR_INVALID_ARGUMENT;
+    if (k > TI_MAX_K) return TI_ERR_UNSUPPORTED;
+    L.n_mod = n_moduli_exact(k, bits);
+    if (L.n_mod < 0 || L.n_mod > kMaxModuli) return TI_ERR_UNSUPPORTED;
+    L.ldk = round_up(k > 0 ? k : 1, 16);
+    L.ldr = round_up(n > 0 ? n : 1, 16);
+    size_t off = 0;
+    L.off_rexp = off; off += align256(sizeof(int32_t) * size_t(m));
+    L.off_cexp = off; off += align256(sizeof(int32_t) * size_t(n));
+    L.off_a = off; off += align256(size_t(L.n_mod) * size_t(m) * size_t(L.ldk));
+    L.off_b = off; off += align256(size_t(L.n_mod) * size_t(n) * size_t(L.ldk));
+    L.off_r = off; off += align256(size_t(L.n_mod) * size_t(m) * size_t(L.ldr));
+    L.total = off;
+    return TI_OK;
+}
+
+int ti_crt_workspace_size(int64_t m, int64_t n, int64_t k, int bits, size_t *bytes) {
+    if (!bytes) return TI_ERR_INVALID_ARGUMENT;
+    CrtLayout L;
+    const int rc = crt_layout(m, n, k, bits, L);
+    if (rc != TI_OK) return rc;
+    *bytes = L.total;
+    return TI_OK;
+}
+
+int ti_crt_split(const double *X, int64_t outer, int64_t kdim, int64_t s_outer, int64_t s_k,
+                 int bits, int n_mod, int32_t *exp_out, int8_t *res_out, int64_t ld_res,
+                 void *stream) {
+    if (outer < 0 || kdim < 1 || n_mod < 1 || n_mod > 30) return TI_ERR_INVALID_ARGUMENT;
+    if (bits < 1 || bits > 53) return TI_ERR_INVALID_ARGUMENT;
+    if (ld_res < kdim || (ld_res & 15) || (reinterpret_cast<uintptr_t>(res_out) & 15))
+        return TI_ERR_INVALID_ARGUMENT;
+    if (!(s_k == 1 || s_outer == 1)) return TI_ERR_INVALID_ARGUMENT;
+    if (outer == 0) return TI_OK;
+    if (!X || !exp_out || !res_out) return TI_ERR_INVALID_ARGUMENT;
+    DevInfo d;
+    int rc = device_info(d);
+    if (rc != TI_OK) return rc;
+    SplitConst C;
+    if (!make_split_const(n_mod, bits, C)) return TI_ERR_INVALID_ARGUMENT;
+    // s_k == 1 selects the k-contiguous kernels (also for a 1-long outer stride)
+    const int64_t sk = (s_k == 1) ? 1 : s_k;
+    const int64_t so = (s_k == 1) ? s_outer : 1;
+    return cuda_status(launch_split(X, outer, kdim, so, sk, C, exp_out, res_out, ld_res,
+                                    d.num_sms, static_cast<cudaStream_t>(stream)));
+}
+
+int ti_batched_gemm_workspace_size(int64_t batch, int64_t M, int64_t K, int64_t N,
+                                   size_t *bytes) {
+    if (!bytes || batch < 0 || M < 0 || K < 0 || N < 0) return TI_ERR_INVALID_ARGUMENT;
+    const int64_t ld = round_up(K > 0 ? K : 1, 16);
+    *bytes = align256(size_t(batch) * size_t(M) * size_t(ld)) +
+             align256(size_t(batch) * size_t(N) * size_t(ld));
+    return TI_OK;
+}
+
+int ti_batched_int8_gemm_mod(const int8_t *a, const int8_t *b, const int32_t *moduli,
+                             int64_t batch, int64_t M, int64_t K, int64_t N, int32_t *c,
+                             void *workspace, size_t workspace_bytes, void *stream) {
+    if (batch < 0 || M < 0 || K < 0 || N < 0) return TI_ERR_INVALID_ARGUMENT;
+    if (batch > kMaxModuli) return TI_ERR_UNSUPPORTED;
+    if (K > 131071) return TI_ERR_UNSUPPORTED;  // 128*128*K < 2^31
+    if (batch == 0 || M == 0 || N == 0) return TI_OK;
+    if (!a || !b || !moduli || !c) return TI_ERR_INVALID_ARGUMENT;
+    ModMagic mm;
+    if (!make_magic(moduli, static_cast<int>(batch), mm)) return TI_ERR_INVALID_ARGUMENT;
+    DevInfo d;
+    int rc = device_info(d);
+    if (rc != TI_OK) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (K == 0) return cuda_status(cudaMemsetAsync(c, 0, sizeof(int32_t) * batch * M * N, s));
+    size_t need = 0;
+    ti_batched_gemm_workspace_size(batch, M, K, N, &need);
+    if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255))
+        return TI_ERR_WORKSPACE;
+    const int64_t ld = round_up(K, 16);
+    int8_t *ap = static_cast<int8_t *>(workspace);
+    int8_t *bp = ap + align256(size_t(batch) * size_t(M) * size_t(ld));
+    {
+        const int64_t total = batch * M * ld;
+        int64_t blocks = (total + 255) / 256;
+        if (blocks > int64_t(d.num_sms) * 8) blocks = int64_t(d.num_sms) * 8;
+        pad_rows_i8_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(a, batch, M, K, ap, ld);
+        int64_t tb = batch * ((ld + 63) / 64) * ((N + 63) / 64);
+        if (tb > int64_t(d.num_sms) * 8) tb = int64_t(d.num_sms) * 8;
+        transpose_i8_kernel<<<static_cast<unsigned>(tb), 256, 0, s>>>(b, batch, K, N, bp, ld);
+        if (cudaGetLastError() != cudaSuccess) return TI_ERR_CUDA;
+    }
+    return cuda_status(launch_residue_gemm(ap, bp, M, N, K, ld, static_cast<int>(batch), mm, c,
+                                           N, 1, d.err, d.num_sms, s));
+}
+
+int ti_crt_reconstruct(const int32_t *residues, const int32_t *moduli, int n_mod, int bits,
+                       const int32_t *row_exp, const int32_t *col_exp, int64_t rows,
+                       int64_t cols, double *out, int64_t ldo, void *stream) {
+    if (rows < 0 || cols < 0 || n_mod < 1 || n_mod > kMaxModuli || ldo < cols)
+        return TI_ERR_INVALID_ARGUMENT;
+    if (bits < 1 || bits > 53) return TI_ERR_INVALID_ARGUMENT;
+    if (rows == 0 || cols == 0) return TI_OK;
+    if (!residues || !moduli || !row_exp || !col_exp || !out) return TI_ERR_INVALID_ARGUMENT;
+    CrtConst K;
+    if (!make_crt_const(moduli, n_mod, bits, K)) return TI_ERR_INVALID_ARGUMENT;
+    DevInfo d;
+    int rc = device_info(d);
+    if (rc != TI_OK) return rc;
+    return cuda_status(launch_crt(residues, false, cols, rows * cols, rows, cols, row_exp, col_exp,
+                                  out, ldo, 0, K, d.num_sms, static_cast<cudaStream_t>(stream)));
+}
+
+static void record(void *const *ev, int i, cudaStream_t s) {
+    if (ev && ev[i]) cudaEventRecord(static_cast<cudaEvent_t>(ev[i]), s);
+}
+
+int ti_crt_matmul(const double *A, int64_t sa0, int64_t sa1, const double *B, int64_t sb0,
+                  int64_t sb1, double *C, int64_t ldc, int64_t m, int64_t n, int64_t k,
+                  int bits, int out_mode, void *workspace, size_t workspace_bytes,
+                  void *stream) {
+    return ti_crt_matmul_events(A, sa0, sa1, B, sb0, sb1, C, ldc, m, n, k, bits, out_mode,
+                                workspace, workspace_bytes, stream, nullptr);
+}
+
+int ti_crt_matmul_events(const double *A, int64_t sa0, int64_t sa1, const double *B,
+                         int64_t sb0, int64_t sb1, double *C, int64_t ldc, int64_t m, int64_t n,
+                         int64_t k, int bits, int out_mode, void *workspace,
+                         size_t workspace_bytes, void *stream, void *const *ev) {
+    if (out_mode < TI_OUT_STORE || out_mode > TI_OUT_ADD) return TI_ERR_INVALID_ARGUMENT;
+    CrtLayout L;
+    int rc = crt_layout(m, n, k, bits, L);
+    if (rc != TI_OK) return rc;
+    if (m == 0 || n == 0) return TI_OK;
+    if (!C || ldc < n) return TI_ERR_INVALID_ARGUMENT;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    DevInfo d;
+    rc = device_info(d);
+    if (rc != TI_OK) return rc;
+    if (k == 0) {  // empty sum: C = 0 (store) or C unchanged
+        if (out_mode != TI_OUT_STORE) return TI_OK;
+        return cuda_status(cudaMemset2DAsync(C, sizeof(double) * ldc, 0, sizeof(double) * n, m, s));
+    }
+    if (!A || !B) return TI_ERR_INVALID_ARGUMENT;
+    if (!(sa1 == 1 || sa0 == 1) || !(sb0 == 1 || sb1 == 1)) return TI_ERR_INVALID_ARGUMENT;
+    if (!workspace || workspace_bytes < L.total || (reinterpret_cast<uintptr_t>(workspace) & 255))
+        return TI_ERR_WORKSPACE;
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    int32_t *rexp = reinterpret_cast<int32_t *>(ws + L.off_rexp);
+    int32_t *cexp = reinterpret_cast<int32_t *>(ws + L.off_cexp);
+    int8_t *ares = reinterpret_cast<int8_t *>(ws + L.off_a);
+    int8_t *bres = reinterpret_cast<int8_t *>(ws + L.off_b);
+    uint8_t *R = ws + L.off_r;
+
+    SplitConst SC;
+    CrtConst KC;
+    if (!make_split_const(L.n_mod, bits, SC)) return TI_ERR_UNSUPPORTED;
+    if (!make_crt_const(kPrimes, L.n_mod, bits, KC)) return TI_ERR_UNSUPPORTED;
+
+    // K1: A as m vectors along k (rows), B as n vectors along k (columns)
+    cudaError_t e;
+    record(ev, 0, s);
+    if (sa1 == 1) e = launch_split(A, m, k, sa0, 1, SC, rexp, ares, L.ldk, d.num_sms, s);
+    else e = launch_split(A, m, k, 1, sa1, SC, rexp, ares, L.ldk, d.num_sms, s);
+    if (e != cudaSuccess) return TI_ERR_CUDA;
+    if (sb0 == 1) e = launch_split(B, n, k, sb1, 1, SC, cexp, bres, L.ldk, d.num_sms, s);
+    else e = launch_split(B, n, k, 1, sb0, SC, cexp, bres, L.ldk, d.num_sms, s);
+    if (e != cudaSuccess) return TI_ERR_CUDA;
+    // K2: per-modulus residue GEMMs, mod-reduced to uint8 planes
+    record(ev, 1, s);
+    e = launch_residue_gemm(ares, bres, m, n, k, L.ldk, L.n_mod, SC.mm, R, L.ldr, 0, d.err,
+                            d.num_sms, s);
+    if (e != cudaSuccess) return e == cudaErrorInvalidValue ? TI_ERR_NO_DEVICE : TI_ERR_CUDA;
+    // K3: exact CRT + inverse scaling
+    record(ev, 2, s);
+    e = launch_crt(R, true, L.ldr, m * L.ldr, m, n, rexp, cexp, C, ldc, out_mode, KC, d.num_sms, s);
+    record(ev, 3, s);
+    return cuda_status(e);
+}
+
+int ti_device_error(int *code_out, int reset) {
+    if (!code_out) return TI_ERR_INVALID_ARGUMENT;
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)) != cudaSuccess) return TI_ERR_CUDA;
+    *code_out = v;
+    if (reset) {
+        const int z = 0;
+        if (cudaMemcpyToSymbol(g_device_error, &z, sizeof(int)) != cudaSuccess) return TI_ERR_CUDA;
+    }
+    return TI_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,222 @@
+// ti_common.cuh -- shared device helpers for the sm_100a CRT matmul kernels.
+//
+// Holds the per-modulus constant blocks passed to every kernel by value, the exact small
+// modular reductions, and thin inline-PTX wrappers for mbarriers, TMA and tcgen05 (TMEM
+// allocation, UMMA issue/commit, TMEM loads).  All waits are bounded by wall time
+// (%globaltimer) so a broken pipeline reports an error instead of hanging the GPU.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ti {
+
+constexpr int kMaxModuli = 32;
+constexpr int kNonfiniteExp = (-2147483647 - 1);
+// A kernel wait that lasts this long is treated as a broken pipeline (device error).
+constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;
+
+// Device error codes written to the library's error word.
+enum : int {
+    kErrNone = 0,
+    kErrTimeoutProducer = 0x101,
+    kErrTimeoutMma = 0x102,
+    kErrTimeoutEpilogue = 0x103,
+    kErrTimeoutDrain = 0x104,
+};
+
+// Exact reduction a mod p for a < 2^31 and 3 <= p < 256, p not a power of two:
+// q = floor(a * magic / 2^(32+shift)) with magic = ceil(2^(32+shift)/p), shift = floor(log2 p).
+// The rounding error of the quotient is below a/2^(32+shift) < 2^-(1+shift) < 1/p.
+struct ModMagic {
+    uint32_t p[kMaxModuli];
+    uint32_t magic[kMaxModuli];
+    uint32_t shift[kMaxModuli];
+};
+
+__device__ __forceinline__ uint32_t mod_small(uint32_t a, uint32_t p, uint32_t magic,
+                                              uint32_t shift) {
+    uint32_t q = __umulhi(a, magic) >> shift;
+    return a - q * p;
+}
+
+// Constants of the split (scale + residue) kernels.
+struct SplitConst {
+    int n_mod;
+    int bits;
+    ModMagic mm;
+    uint32_t w32[kMaxModuli];   // 2^32 mod p
+    uint32_t w16[kMaxModuli];   // 2^16 mod p
+    uint32_t bigp[kMaxModuli];  // p * ceil(2^29 / p): a multiple of p that is >= 2^29
+};
+
+// Constants of the CRT reconstruction.  M = prod p_i < 2^127, M_i = M / p_i.
+struct CrtConst {
+    int n_mod;
+    int two_bits;
+    ModMagic mm;
+    uint32_t u[kMaxModuli];        // (M_i)^-1 mod p_i
+    uint32_t finv[kMaxModuli];     // round(2^32 / p_i)
+    uint32_t Mi[kMaxModuli][4];    // M_i, little-endian 32-bit words
+    uint32_t M[4];
+    uint32_t H[4];                 // (M - 1) / 2
+};
+
+// ---------------------------------------------------------------------------------------
+// small PTX helpers
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+                 : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Waits for the phase of `bar` with the given parity to complete.  Returns false when the
+// wait exceeds kWaitTimeoutNs or when another role of the CTA raised *abort.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
+                                          volatile int *abort) {
+    const uint32_t a = smem_u32(bar);
+    if (mbar_try_wait(a, parity)) return true;
+    const unsigned long long t0 = globaltimer_ns();
+    while (true) {
+        if (mbar_try_wait(a, parity)) return true;
+        if (*abort) return false;
+        if (globaltimer_ns() - t0 > kWaitTimeoutNs) return false;
+    }
+}
+
+// 3-D tiled TMA load global -> shared, completing on `bar` (no multicast).
+__device__ __forceinline__ void tma_load_3d(void *smem_dst, const CUtensorMap *map,
+                                            uint64_t *bar, int c0, int c1, int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ---------------------------------------------------------------------------------------
+// tcgen05 (5th-generation tensor cores, TMEM accumulators)
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, int8 x int8 -> int32, shapes from idesc.
+__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                        uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrives on `bar` once every tcgen05.mma previously issued by this thread has completed.
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+            smem_u32(bar))
+        : "memory");
+}
+
+// 32 lanes x 32 columns of 32-bit TMEM words: thread t of the warp receives lane
+// (base_lane + t), columns [col, col+32).
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, "
+        "[%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+          "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor for a K-major operand tile stored with the 128-byte
+// swizzle: rows of 128 bytes, 8-row (1024-byte) swizzle atoms stacked at 1024-byte
+// stride (SBO), descriptor version 1 (sm_100), layout type 2 (SWIZZLE_128B).
+__device__ __forceinline__ uint64_t make_sw128_kmajor_desc(uint32_t saddr) {
+    return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (static_cast<uint64_t>(1) << 16) |
+           (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
+           (static_cast<uint64_t>(2) << 61);
+}
+
+// Instruction descriptor of tcgen05.mma.kind::i8: D s32, A and B signed 8-bit, both
+// K-major, M x N tile.
+__host__ __device__ constexpr uint32_t make_idesc_i8(int M, int N) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
+           (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+}  // namespace ti

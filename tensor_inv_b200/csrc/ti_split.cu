@@ -1,0 +1,266 @@
+// ti_split.cu -- K1: fused power-of-two scaling + int8 residue split of one operand.
+//
+// Restates src/tensor_inv/crt_matmul.py:38-52 (_scale_to_int, _residues) in exact integer
+// arithmetic.  An operand is `outer` vectors of length `kdim` (rows of A or columns of B)
+// with element (o, l) at X[o*s_outer + l*s_k].  Two passes:
+//   1. exponent: e_o = frexp(max(max_l |x_ol|, 1e-300)).exponent (or kNonfiniteExp)
+//   2. split:    v = round_half_even(x * 2^(bits - e_o)) computed from the float64 bits,
+//                r_i = v mod p_i in [0, p_i), written K-major as res[i][o][l] (int8).
+// Two layouts of the source are handled without copies: k contiguous (s_k == 1, "rows")
+// and outer contiguous (s_outer == 1, "cols", a transposed view), the latter through a
+// shared-memory transpose.  Both write 8 consecutive residues per thread and modulus
+// as one 8-byte store, so a warp writes whole 32-byte sectors.
+#include "ti_common.cuh"
+
+namespace ti {
+
+__device__ __forceinline__ uint64_t abs_bits(double x) {
+    return static_cast<uint64_t>(__double_as_longlong(x)) & 0x7FFFFFFFFFFFFFFFull;
+}
+
+// frexp exponent of max(m, 1e-300) from the bit pattern of m = max |x| (non-negative).
+__device__ __forceinline__ int exp_from_maxbits(uint64_t mb) {
+    if (mb >= 0x7FF0000000000000ull) return kNonfiniteExp;  // inf or NaN in the vector
+    if (mb < 0x0010000000000000ull) return -996;             // zero or subnormal: clamp
+    int e = static_cast<int>(mb >> 52) - 1022;               // frexp exponent
+    return e < -996 ? -996 : e;                               // clamp(min=1e-300)
+}
+
+// round_half_even(|x| * 2^(bits - e)) for |x| < 2^e; also returns the sign of x.
+__device__ __forceinline__ uint64_t scaled_magnitude(double x, int bits, int e, bool &neg) {
+    const uint64_t u = static_cast<uint64_t>(__double_as_longlong(x));
+    neg = (u >> 63) != 0;
+    const int be = static_cast<int>((u >> 52) & 0x7FF);
+    const uint64_t f = u & 0x000FFFFFFFFFFFFFull;
+    uint64_t sig;
+    int ex;  // |x| = sig * 2^ex
+    if (be == 0) {
+        sig = f;
+        ex = -1074;
+    } else {
+        sig = f | 0x0010000000000000ull;
+        ex = be - 1075;
+    }
+    int sh = e - bits - ex;  // right shift, >= 0 because |x| < 2^e
+    if (sh <= 0) return sig << (-sh);  // sh == 0 only (kept general)
+    if (sh > 63) sh = 63;              // sig < 2^53: shifts >= 54 all round to zero
+    const uint64_t q = sig >> sh;
+    const uint64_t rem = sig & ((1ull << sh) - 1);
+    const uint64_t half = 1ull << (sh - 1);
+    return q + ((rem > half) || (rem == half && (q & 1)));
+}
+
+// Residue bytes of 8 signed values (magnitudes mag[j] < 2^53, signs neg[j]) mod p_i,
+// packed little-endian into two 32-bit words.
+__device__ __forceinline__ uint2 residues8(const uint32_t (&a2)[8], const uint32_t (&a1)[8],
+                                           const uint32_t (&a0)[8], uint32_t negmask,
+                                           const SplitConst &C, int i) {
+    const uint32_t p = C.mm.p[i], magic = C.mm.magic[i], shift = C.mm.shift[i];
+    const uint32_t w32 = C.w32[i], w16 = C.w16[i], bigp = C.bigp[i];
+    uint32_t out[2] = {0u, 0u};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        // mag = a2*2^32 + a1*2^16 + a0  ==>  t == mag (mod p), t < 2^29
+        uint32_t t = a2[j] * w32 + a1[j] * w16 + a0[j];
+        t = ((negmask >> j) & 1u) ? bigp - t : t;  // -mag (mod p), still < 2^30
+        const uint32_t r = mod_small(t, p, magic, shift);
+        out[j >> 2] |= r << (8 * (j & 3));
+    }
+    return make_uint2(out[0], out[1]);
+}
+
+__device__ __forceinline__ void decompose8(const double (&x)[8], int bits, int e,
+                                           uint32_t (&a2)[8], uint32_t (&a1)[8],
+                                           uint32_t (&a0)[8], uint32_t &negmask) {
+    negmask = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        bool neg;
+        const uint64_t mag = (e == kNonfiniteExp) ? 0ull : scaled_magnitude(x[j], bits, e, neg);
+        if (e == kNonfiniteExp) neg = false;
+        const uint32_t lo = static_cast<uint32_t>(mag);
+        a2[j] = static_cast<uint32_t>(mag >> 32);
+        a1[j] = lo >> 16;
+        a0[j] = lo & 0xFFFFu;
+        negmask |= (neg && mag != 0 ? 1u : 0u) << j;
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// pass 1: exponents
+// ---------------------------------------------------------------------------------------
+
+// k contiguous: one warp per vector.
+__global__ void exp_rows_kernel(const double *__restrict__ X, int64_t outer, int64_t kdim,
+                                int64_t s_outer, int32_t *__restrict__ exp_out) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t o = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+         o < outer; o += warps) {
+        const double *x = X + o * s_outer;
+        uint64_t mb = 0;
+        int64_t l = lane;
+        for (; l + 96 < kdim; l += 128) {
+            const uint64_t b0 = abs_bits(__ldg(x + l)), b1 = abs_bits(__ldg(x + l + 32));
+            const uint64_t b2 = abs_bits(__ldg(x + l + 64)), b3 = abs_bits(__ldg(x + l + 96));
+            mb = max(mb, max(max(b0, b1), max(b2, b3)));
+        }
+        for (; l < kdim; l += 32) mb = max(mb, abs_bits(__ldg(x + l)));
+#pragma unroll
+        for (int off = 16; off; off >>= 1) mb = max(mb, __shfl_xor_sync(0xFFFFFFFFu, mb, off));
+        if (lane == 0) exp_out[o] = exp_from_maxbits(mb);
+    }
+}
+
+// outer contiguous: a 32 x 32 thread block owns 32 vectors, threads stride over k.
+__global__ void exp_cols_kernel(const double *__restrict__ X, int64_t outer, int64_t kdim,
+                                int64_t s_k, int32_t *__restrict__ exp_out) {
+    __shared__ uint64_t red[32][33];
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    const int64_t o = static_cast<int64_t>(blockIdx.x) * 32 + tx;
+    uint64_t mb = 0;
+    if (o < outer) {
+        int64_t l = ty;
+        for (; l + 96 < kdim; l += 128) {
+            const uint64_t b0 = abs_bits(__ldg(X + l * s_k + o));
+            const uint64_t b1 = abs_bits(__ldg(X + (l + 32) * s_k + o));
+            const uint64_t b2 = abs_bits(__ldg(X + (l + 64) * s_k + o));
+            const uint64_t b3 = abs_bits(__ldg(X + (l + 96) * s_k + o));
+            mb = max(mb, max(max(b0, b1), max(b2, b3)));
+        }
+        for (; l < kdim; l += 32) mb = max(mb, abs_bits(__ldg(X + l * s_k + o)));
+    }
+    red[ty][tx] = mb;
+    __syncthreads();
+    if (ty == 0) {
+        for (int r = 1; r < 32; ++r) mb = max(mb, red[r][tx]);
+        if (o < outer) exp_out[o] = exp_from_maxbits(mb);
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// pass 2: scale + residues
+// ---------------------------------------------------------------------------------------
+
+// k contiguous.  Each thread owns 8 consecutive elements of one vector.
+__global__ void __launch_bounds__(256) split_rows_kernel(
+    const double *__restrict__ X, int64_t outer, int64_t kdim, int64_t s_outer,
+    const int32_t *__restrict__ exps, int8_t *__restrict__ res, int64_t ld_res,
+    int64_t plane, const __grid_constant__ SplitConst C) {
+    const int64_t chunks_per_vec = ld_res >> 3;
+    const int64_t total = outer * chunks_per_vec;
+    const bool vec_ok = ((reinterpret_cast<uintptr_t>(X) & 15) == 0) && ((s_outer & 1) == 0);
+    for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t o = idx / chunks_per_vec;
+        const int64_t l0 = (idx - o * chunks_per_vec) << 3;
+        const double *x = X + o * s_outer + l0;
+        double v[8];
+        if (vec_ok && l0 + 8 <= kdim) {
+#pragma unroll
+            for (int j = 0; j < 8; j += 2) {
+                const double2 t = __ldg(reinterpret_cast<const double2 *>(x + j));
+                v[j] = t.x;
+                v[j + 1] = t.y;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = (l0 + j < kdim) ? __ldg(x + j) : 0.0;
+        }
+        const int e = exps[o];
+        uint32_t a2[8], a1[8], a0[8], negmask;
+        decompose8(v, C.bits, e, a2, a1, a0, negmask);
+        int8_t *dst = res + o * ld_res + l0;
+        for (int i = 0; i < C.n_mod; ++i) {
+            const uint2 w = residues8(a2, a1, a0, negmask, C, i);
+            *reinterpret_cast<uint2 *>(dst + i * plane) = w;
+        }
+    }
+}
+
+// outer contiguous (a transposed view).  A block loads a 64 (k) x 32 (outer) tile with
+// coalesced reads, transposes it through shared memory, and each thread then owns 8
+// consecutive k of one vector.
+constexpr int kColTileK = 64, kColTileO = 32, kColPad = 66;  // row pitch in doubles
+
+__global__ void __launch_bounds__(256) split_cols_kernel(
+    const double *__restrict__ X, int64_t outer, int64_t kdim, int64_t s_k,
+    const int32_t *__restrict__ exps, int8_t *__restrict__ res, int64_t ld_res,
+    int64_t plane, const __grid_constant__ SplitConst C) {
+    __shared__ __align__(16) double tile[kColTileO * kColPad];  // [o][k]
+    const int tid = threadIdx.x;
+    const int64_t tiles_o = (outer + kColTileO - 1) / kColTileO;
+    const int64_t tiles_k = (ld_res + kColTileK - 1) / kColTileK;
+    for (int64_t t = blockIdx.x; t < tiles_o * tiles_k; t += gridDim.x) {
+        const int64_t to = t / tiles_k, tk = t - to * tiles_k;
+        const int64_t o0 = to * kColTileO, l0 = tk * kColTileK;
+        {   // coalesced load: warp w reads rows l0 + w + 8r, 32 consecutive outer indices
+            const int tx = tid & 31, ty = tid >> 5;
+            const int64_t o = o0 + tx;
+#pragma unroll
+            for (int r = 0; r < kColTileK / 8; ++r) {
+                const int64_t l = l0 + ty + 8 * r;
+                tile[tx * kColPad + ty + 8 * r] =
+                    (o < outer && l < kdim) ? __ldg(X + l * s_k + o) : 0.0;
+            }
+        }
+        __syncthreads();
+        const int oo = tid >> 3, kc = tid & 7;
+        const int64_t o = o0 + oo;
+        const int64_t lc = l0 + kc * 8;
+        if (o < outer && lc < ld_res) {
+            double v[8];
+            const double2 *src = reinterpret_cast<const double2 *>(tile + oo * kColPad + kc * 8);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const double2 d = src[j];
+                v[2 * j] = d.x;
+                v[2 * j + 1] = d.y;
+            }
+            const int e = exps[o];
+            uint32_t a2[8], a1[8], a0[8], negmask;
+            decompose8(v, C.bits, e, a2, a1, a0, negmask);
+            int8_t *dst = res + o * ld_res + lc;
+            for (int i = 0; i < C.n_mod; ++i) {
+                const uint2 w = residues8(a2, a1, a0, negmask, C, i);
+                *reinterpret_cast<uint2 *>(dst + i * plane) = w;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// host launchers
+// ---------------------------------------------------------------------------------------
+cudaError_t launch_split(const double *X, int64_t outer, int64_t kdim, int64_t s_outer,
+                         int64_t s_k, const SplitConst &C, int32_t *exp_out, int8_t *res,
+                         int64_t ld_res, int num_sms, cudaStream_t stream) {
+    if (outer == 0) return cudaSuccess;
+    const int64_t plane = outer * ld_res;
+    if (s_k == 1) {
+        const int64_t warps_needed = outer;
+        int64_t blocks = (warps_needed + 7) / 8;
+        if (blocks > int64_t(num_sms) * 16) blocks = int64_t(num_sms) * 16;
+        exp_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(X, outer, kdim,
+                                                                           s_outer, exp_out);
+        const int64_t total = outer * (ld_res >> 3);
+        int64_t sblocks = (total + 255) / 256;
+        if (sblocks > int64_t(num_sms) * 8) sblocks = int64_t(num_sms) * 8;
+        split_rows_kernel<<<static_cast<unsigned>(sblocks), 256, 0, stream>>>(
+            X, outer, kdim, s_outer, exp_out, res, ld_res, plane, C);
+    } else {
+        const int64_t blocks = (outer + 31) / 32;
+        exp_cols_kernel<<<static_cast<unsigned>(blocks), 1024, 0, stream>>>(X, outer, kdim, s_k,
+                                                                            exp_out);
+        const int64_t tiles = ((outer + kColTileO - 1) / kColTileO) *
+                              ((ld_res + kColTileK - 1) / kColTileK);
+        int64_t sblocks = tiles;
+        if (sblocks > int64_t(num_sms) * 8) sblocks = int64_t(num_sms) * 8;
+        split_cols_kernel<<<static_cast<unsigned>(sblocks), 256, 0, stream>>>(
+            X, outer, kdim, s_k, exp_out, res, ld_res, plane, C);
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace ti

@@ -1,0 +1,20 @@
+"""The reference's tests/test_cholesky.py, run against tensor_inv_b200."""
+import pytest
+import torch
+
+from tensor_inv_b200.cholesky import cholesky
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("device", ["cpu", "cuda"])
+def test_cholesky(device):
+    torch.manual_seed(42)
+    n = 128
+    A = torch.randn(n, n, dtype=torch.float64)
+    A = (A @ A.T + n * torch.eye(n, dtype=torch.float64)).to(device)  # SPD
+
+    L = cholesky(A, block_size=32)
+    err = (L @ L.T - A).abs().max().item()
+    assert err < 1e-8, f"reconstruction error {err:.2e}"
+    assert (torch.diag(L) > 0).all(), "diagonal should be positive"

@@ -1,0 +1,244 @@
+"""Parity of the sm_100a CRT matmul with the reference (golden fixtures) and the oracle.
+
+Bit-exact throughout: float64 outputs are compared as uint64 bit patterns, residues and
+exponents as integers.  Sizes stay where the C oracle answers in seconds; beyond that,
+sub-blocks of a large product are checked (row exponents depend only on A's rows and
+column exponents only on B's columns, so every output block of the full product equals
+the product of the matching panels).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN, golden_cases
+
+pytestmark = pytest.mark.gpu
+
+DTYPES = {"float64": torch.float64, "float32": torch.float32, "float16": torch.float16,
+          "bfloat16": torch.bfloat16}
+
+
+def _bits(t):
+    return t.detach().cpu().contiguous().view(torch.int64).numpy()
+
+
+def _assert_bitexact(got, want):
+    got = got.detach().cpu().to(torch.float64).contiguous()
+    want = np.ascontiguousarray(want, np.float64)
+    g, w = got.numpy().view(np.uint64), want.view(np.uint64)
+    if not np.array_equal(g, w):
+        bad = np.argwhere(g != w)
+        i, j = bad[0]
+        raise AssertionError(f"{len(bad)} mismatches; first at {(i, j)}: got "
+                             f"{got.numpy()[i, j]!r} want {want[i, j]!r}")
+
+
+@pytest.fixture(scope="module")
+def ti():
+    import tensor_inv_b200
+
+    assert torch.cuda.is_available()
+    return tensor_inv_b200
+
+
+@pytest.fixture(autouse=True)
+def _no_device_error():
+    from tensor_inv_b200 import _native
+
+    yield
+    torch.cuda.synchronize()
+    assert _native.device_error(reset=True) == 0
+
+
+def _golden(case):
+    return dict(np.load(GOLDEN / f"{case}.npz"))
+
+
+@pytest.mark.parametrize("case", golden_cases())
+def test_golden_full_path(ti, case):
+    g = _golden(case)
+    dt = DTYPES[str(g["dtype"])]
+    A = torch.from_numpy(g["A"]).to(dt).cuda()
+    B = torch.from_numpy(g["B"]).to(dt).cuda()
+    C = ti.crt_matmul(A, B)
+    assert C.dtype == torch.float64 and C.is_cuda
+    _assert_bitexact(C, g["out"])
+
+
+@pytest.mark.parametrize("case", golden_cases())
+def test_golden_stages(ti, case):
+    from tensor_inv_b200 import crt_matmul as cm
+
+    g = _golden(case)
+    bits, moduli = int(g["bits"]), [int(p) for p in g["moduli"]]
+    A = torch.from_numpy(g["A"]).cuda()
+    B = torch.from_numpy(g["B"]).cuda()
+    re, ares = cm._split(A, bits, len(moduli), axis_k=1)
+    ce, bres = cm._split(B, bits, len(moduli), axis_k=0)
+    np.testing.assert_array_equal(re.cpu().numpy(), g["row_exp"])
+    np.testing.assert_array_equal(ce.cpu().numpy(), g["col_exp"])
+    np.testing.assert_array_equal(ares.cpu().numpy(), g["a_res"])
+    np.testing.assert_array_equal(bres.cpu().numpy().transpose(0, 2, 1), g["b_res"])
+    # residue GEMM on the reference's own residues, reference layout
+    c = cm._matmul_residues(torch.from_numpy(g["a_res"]).cuda(),
+                            torch.from_numpy(g["b_res"]).cuda(), moduli)
+    np.testing.assert_array_equal(torch.stack(c).cpu().numpy(), g["c_res"])
+    # CRT on the reference's own residue products
+    out = cm._crt_reconstruct(torch.from_numpy(g["c_res"]).cuda(), moduli, bits,
+                              torch.from_numpy(g["row_exp"]), torch.from_numpy(g["col_exp"]))
+    _assert_bitexact(out, g["out"])
+
+
+def _rand(shape, seed, phi=None, dtype=torch.float64):
+    gen = torch.Generator().manual_seed(seed)
+    if phi is None:
+        x = torch.randn(*shape, generator=gen, dtype=torch.float64)
+    else:
+        u = torch.rand(*shape, generator=gen, dtype=torch.float64) - 0.5
+        x = u * torch.exp(phi * torch.randn(*shape, generator=gen, dtype=torch.float64))
+    return x.to(dtype)
+
+
+SHAPES = [
+    (1024, 1024, 1024, None),   # BASELINE config 1 shape, N(0,1)
+    (300, 500, 257, 2.0),
+    (129, 257, 1, None),
+    (133, 77, 1100, 1.0),
+    (1, 300, 40, None),
+    (257, 1, 129, 0.5),
+    (128, 256, 128, None),      # exactly one tile
+    (200, 600, 7200, 0.5),      # N = 25 moduli
+]
+
+
+@pytest.mark.parametrize("m,n,k,phi", SHAPES)
+def test_vs_oracle(ti, oracle, m, n, k, phi):
+    A = _rand((m, k), 1000 + m, phi)
+    B = _rand((k, n), 2000 + n, phi)
+    want = oracle.crt_matmul(A.numpy(), B.numpy(), 53)
+    _assert_bitexact(ti.crt_matmul(A.cuda(), B.cuda()), want)
+
+
+@pytest.mark.parametrize("ta,tb", [(True, False), (False, True), (True, True)])
+def test_transposed_views(ti, oracle, ta, tb):
+    m, n, k = 190, 150, 333
+    A = _rand((k, m), 7, 1.0).T if ta else _rand((m, k), 7, 1.0)
+    B = _rand((n, k), 8, 1.0).T if tb else _rand((k, n), 8, 1.0)
+    want = oracle.crt_matmul(A.numpy(), B.numpy(), 53)
+    _assert_bitexact(ti.crt_matmul(A.cuda(), B.cuda()), want)
+
+
+def test_strided_view_is_copied(ti, oracle):
+    A = _rand((120, 300), 3)[:, ::3]      # neither stride is 1
+    B = _rand((100, 90), 4)
+    want = oracle.crt_matmul(A.numpy(), B.numpy(), 53)
+    _assert_bitexact(ti.crt_matmul(A.cuda(), B.cuda()), want)
+
+
+@pytest.mark.parametrize("dtype,bits", [(torch.float32, 24), (torch.bfloat16, 8),
+                                        (torch.float16, 11)])
+def test_reduced_precision(ti, oracle, dtype, bits):
+    A = _rand((150, 700), 11, 0.5, dtype)
+    B = _rand((700, 130), 12, 0.5, dtype)
+    want = oracle.crt_matmul(A.double().numpy(), B.double().numpy(), bits)
+    _assert_bitexact(ti.crt_matmul(A.cuda(), B.cuda()), want)
+
+
+def test_cpu_inputs_round_trip(ti, oracle):
+    A = _rand((37, 51), 42)
+    B = _rand((51, 29), 43)
+    C = ti.crt_matmul(A, B)
+    assert C.device.type == "cpu"
+    _assert_bitexact(C, oracle.crt_matmul(A.numpy(), B.numpy(), 53))
+
+
+@pytest.mark.parametrize("alpha", [-1, 1])
+def test_fused_update(ti, oracle, alpha):
+    m, n, k = 300, 270, 256
+    A = _rand((m, k), 21)
+    B = _rand((k, n), 22)
+    C0 = _rand((m, n), 23)
+    prod = oracle.crt_matmul(A.numpy(), B.numpy(), 53)
+    want = C0.numpy() - prod if alpha == -1 else C0.numpy() + prod
+    C = C0.cuda()
+    ti.crt_matmul_update(C, A.cuda(), B.cuda(), alpha=alpha)
+    _assert_bitexact(C, want)
+
+
+def test_update_on_submatrix_view(ti, oracle):
+    W = _rand((400, 400), 31)
+    want = W.numpy().copy()
+    want[100:, 100:] -= oracle.crt_matmul(W.numpy()[100:, 36:100], W.numpy()[36:100, 100:], 53)
+    Wd = W.cuda()
+    ti.crt_matmul_update(Wd[100:, 100:], Wd[100:, 36:100], Wd[36:100, 100:], alpha=-1)
+    _assert_bitexact(Wd, want)
+
+
+def test_nonfinite_rows_and_cols(ti, oracle):
+    A = _rand((40, 60), 51)
+    B = _rand((60, 30), 52)
+    A[3, 7] = float("nan")
+    A[9, 0] = float("inf")
+    B[5, 11] = float("-inf")
+    C = ti.crt_matmul(A.cuda(), B.cuda()).cpu()
+    assert torch.isnan(C[3]).all() and torch.isnan(C[9]).all() and torch.isnan(C[:, 11]).all()
+    keep_r = [i for i in range(40) if i not in (3, 9)]
+    keep_c = [j for j in range(30) if j != 11]
+    want = oracle.crt_matmul(A[keep_r].numpy(), B[:, keep_c].numpy(), 53)
+    _assert_bitexact(C[keep_r][:, keep_c], want)
+
+
+def test_overflow_gives_inf(ti):
+    # the reference raises OverflowError from math.ldexp; the kernel returns +-inf
+    A = torch.full((2, 4), 1e200, dtype=torch.float64)
+    B = torch.full((4, 2), 1e200, dtype=torch.float64)
+    C = ti.crt_matmul(A.cuda(), B.cuda()).cpu()
+    assert torch.isinf(C).all() and (C > 0).all()
+
+
+def test_large_blocks_vs_oracle(ti, oracle):
+    """4096^3 product; three output blocks checked bit for bit against panel products."""
+    m = n = k = 4096
+    A = _rand((m, k), 61, 1.0)
+    B = _rand((k, n), 62, 1.0)
+    C = ti.crt_matmul(A.cuda(), B.cuda()).cpu()
+    for (r0, r1, c0, c1) in [(0, 96, 0, 80), (4000, 4096, 4017, 4096), (1234, 1300, 2900, 3000)]:
+        want = oracle.crt_matmul(A[r0:r1].numpy(), B[:, c0:c1].numpy(), 53)
+        _assert_bitexact(C[r0:r1, c0:c1], want)
+
+
+def test_residue_gemm_signed_inputs(ti, oracle):
+    """The reference-layout GEMM entry point accepts any int8 and any modulus in [2, 256)."""
+    from tensor_inv_b200 import crt_matmul as cm
+
+    gen = torch.Generator().manual_seed(5)
+    a = torch.randint(-128, 128, (4, 70, 300), generator=gen, dtype=torch.int8)
+    b = torch.randint(-128, 128, (4, 300, 50), generator=gen, dtype=torch.int8)
+    moduli = [3, 251, 128, 97]
+    got = torch.stack(cm._matmul_residues(a.cuda(), b.cuda(), moduli)).cpu().numpy()
+    want = oracle.residue_gemm(a.numpy(), b.numpy(), moduli)
+    np.testing.assert_array_equal(got, want)
+
+
+def test_errors(ti):
+    A = torch.randn(4, 5, dtype=torch.float64, device="cuda")
+    with pytest.raises(TypeError):
+        ti.crt_matmul(A.int(), A.int())
+    with pytest.raises(IndexError):
+        ti.crt_matmul(A[:, :0], A[:0])
+    with pytest.raises(RuntimeError):
+        ti.crt_matmul(A, A)
+    with pytest.raises(ValueError):
+        from tensor_inv_b200.crt_matmul import _n_moduli
+        _n_moduli(2**62, 53)
+    with pytest.raises(RuntimeError):
+        big = torch.zeros(1, 135264, dtype=torch.float64, device="cuda")
+        ti.crt_matmul(big, big.T)
+
+
+def test_empty_outputs(ti):
+    A = torch.randn(0, 5, dtype=torch.float64, device="cuda")
+    B = torch.randn(5, 3, dtype=torch.float64, device="cuda")
+    assert ti.crt_matmul(A, B).shape == (0, 3)
+    assert ti.crt_matmul(B.T, B[:, :0]).shape == (3, 0)
