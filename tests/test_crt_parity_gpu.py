@@ -7,6 +7,8 @@ column exponents only on B's columns, so every output block of the full product 
 the product of the matching panels).
 """
 
+import importlib
+
 import numpy as np
 import pytest
 import torch
@@ -68,7 +70,7 @@ def test_golden_full_path(ti, case):
 
 @pytest.mark.parametrize("case", golden_cases())
 def test_golden_stages(ti, case):
-    from tensor_inv_b200 import crt_matmul as cm
+    cm = importlib.import_module("tensor_inv_b200.crt_matmul")
 
     g = _golden(case)
     bits, moduli = int(g["bits"]), [int(p) for p in g["moduli"]]
@@ -210,7 +212,7 @@ def test_large_blocks_vs_oracle(ti, oracle):
 
 def test_residue_gemm_signed_inputs(ti, oracle):
     """The reference-layout GEMM entry point accepts any int8 and any modulus in [2, 256)."""
-    from tensor_inv_b200 import crt_matmul as cm
+    cm = importlib.import_module("tensor_inv_b200.crt_matmul")
 
     gen = torch.Generator().manual_seed(5)
     a = torch.randint(-128, 128, (4, 70, 300), generator=gen, dtype=torch.int8)
