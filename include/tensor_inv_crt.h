@@ -37,7 +37,8 @@ typedef enum {
     TI_ERR_WORKSPACE = 3,        /* workspace too small or misaligned */
     TI_ERR_CUDA = 4,             /* a CUDA runtime/driver call failed */
     TI_ERR_DEVICE_TIMEOUT = 5,   /* a kernel gave up on a bounded wait (see ti_device_error) */
-    TI_ERR_NO_DEVICE = 6         /* no sm_100 device, or the driver entry point is missing */
+    TI_ERR_NO_DEVICE = 6,        /* no sm_100 device, or the driver entry point is missing */
+    TI_ERR_SCRATCH_LIMIT = 7     /* problem needs more than ti_crt_matmul_noalloc's scratch */
 } ti_status_t;
 
 /* Row/column exponent value that marks a row of A (or column of B) holding a NaN or an
@@ -134,6 +135,25 @@ int ti_crt_matmul_events(const double *A, int64_t sa0, int64_t sa1, const double
                          int64_t sb0, int64_t sb1, double *C, int64_t ldc, int64_t m, int64_t n,
                          int64_t k, int bits, int out_mode, void *workspace,
                          size_t workspace_bytes, void *stream, void *const *stage_events);
+
+/* Bytes of the library's static device scratch used by ti_crt_matmul_noalloc (64 MiB). */
+#define TI_NOALLOC_SCRATCH_BYTES ((size_t)64 << 20)
+
+/*
+ * ti_crt_matmul without a workspace, for callers that cannot allocate device memory: a host
+ * program whose own allocator already owns the GPU's memory pool, or a latency-critical
+ * caller that cannot afford cudaMalloc's implicit device synchronisation.  No counterpart
+ * in the reference (its crt_matmul allocates through torch).  It calls no cudaMalloc,
+ * cudaFree or allocating library routine; its scratch is a static device array of
+ * TI_NOALLOC_SCRATCH_BYTES per device, held by every GPU that loads it until the process
+ * exits.  Problems whose ti_crt_workspace_size() exceeds that return TI_ERR_SCRATCH_LIMIT
+ * (about m = n = k = 940 at float64).  The first call on each device looks up the array's
+ * device address and should come before any stream capture.  All calls on a device share
+ * the array: calls that overlap on the GPU race and must be serialised by the caller.
+ */
+int ti_crt_matmul_noalloc(const double *A, int64_t sa0, int64_t sa1, const double *B,
+                          int64_t sb0, int64_t sb1, double *C, int64_t ldc, int64_t m, int64_t n,
+                          int64_t k, int bits, int out_mode, void *stream);
 
 /*
  * Reads (and, if reset != 0, clears) the current device's kernel error word.  Kernels set

@@ -19,6 +19,7 @@ TI_ERR_WORKSPACE = 3
 TI_ERR_CUDA = 4
 TI_ERR_DEVICE_TIMEOUT = 5
 TI_ERR_NO_DEVICE = 6
+TI_ERR_SCRATCH_LIMIT = 7
 
 TI_OUT_STORE = 0
 TI_OUT_SUBTRACT = 1
@@ -43,6 +44,8 @@ SIGNATURES = {
                              _int, _p, _sz, _p]),
     "ti_crt_matmul_events": (_int, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i64, _i64,
                                     _int, _int, _p, _sz, _p, _p]),
+    "ti_crt_matmul_noalloc": (_int, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i64,
+                                     _i64, _int, _int, _p]),
     "ti_device_error": (_int, [ctypes.POINTER(_int), _int]),
 }
 

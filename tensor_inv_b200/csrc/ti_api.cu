@@ -221,6 +221,8 @@ const char *ti_status_string(int status) {
         case TI_ERR_CUDA: return "CUDA error";
         case TI_ERR_DEVICE_TIMEOUT: return "device wait timed out";
         case TI_ERR_NO_DEVICE: return "no sm_100 device";
+        case TI_ERR_SCRATCH_LIMIT:
+            return "problem needs more scratch than the no-alloc entry point's static 64 MiB";
         default: return "unknown status";
     }
 }
