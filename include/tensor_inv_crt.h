@@ -106,6 +106,36 @@ int ti_crt_reconstruct(const int32_t *residues, const int32_t *moduli, int n_mod
                        const int32_t *row_exp, const int32_t *col_exp, int64_t rows,
                        int64_t cols, double *out, int64_t ldo, void *stream);
 
+/* Moduli sets.  TI_MODULI_PRIMES is the reference's (the first N odd primes, 3..127,
+   N from _n_moduli).  TI_MODULI_WIDE is the opt-in extension of the survey's config 2:
+   pairwise-coprime odd moduli up to 255 (255, 253, 251, 247, 241, 239, 233, 229, 227, 223,
+   217, 211, 199, 197, 193, 191), at most 16.  With the automatic count, WIDE keeps every
+   bit of the input precision, so its outputs are bit-identical to PRIMES with about a
+   third fewer residue GEMMs (16 instead of 25 at k = 8192). */
+#define TI_MODULI_PRIMES 0
+#define TI_MODULI_WIDE 1
+
+/* Options of the *_ex entry points.  A NULL options pointer means all defaults. */
+typedef struct ti_crt_options {
+    int moduli;             /* TI_MODULI_PRIMES (default) or TI_MODULI_WIDE */
+    int n_moduli;           /* 0: automatic (PRIMES: the reference's _n_moduli; WIDE: the
+                               fewest moduli that keep `bits`).  Otherwise exactly this many
+                               (PRIMES <= 25, WIDE <= 16); when they cannot hold 2*k*2^(2*bits)
+                               the precision is lowered to the largest b with
+                               prod(moduli) > 2*k*2^(2*b), the config-2 moduli sweep */
+    void *stage_events[4];  /* optional cudaEvent_t, recorded on the stream before K1, before
+                               K2, before K3 and after K3; NULL entries are skipped */
+} ti_crt_options_t;
+
+/* The moduli count, the precision actually kept, and (if moduli_out != NULL, room for 32)
+   the moduli that ti_crt_matmul_ex will use for inner dimension k at `bits`. */
+int ti_crt_plan(int64_t k, int bits, const ti_crt_options_t *opt, int *n_mod_out,
+                int *bits_eff_out, int32_t *moduli_out);
+
+/* Workspace bytes of ti_crt_matmul_ex with these options. */
+int ti_crt_workspace_size_ex(int64_t m, int64_t n, int64_t k, int bits,
+                             const ti_crt_options_t *opt, size_t *bytes);
+
 /* Output modes of ti_crt_matmul. */
 #define TI_OUT_STORE 0    /* C  = A @ B  */
 #define TI_OUT_SUBTRACT 1 /* C -= A @ B  (C - round(A@B), as `W -= crt_matmul(...)`) */
@@ -124,6 +154,16 @@ int ti_crt_matmul(const double *A, int64_t sa0, int64_t sa1, const double *B, in
                   int64_t sb1, double *C, int64_t ldc, int64_t m, int64_t n, int64_t k,
                   int bits, int out_mode, void *workspace, size_t workspace_bytes,
                   void *stream);
+
+/*
+ * ti_crt_matmul with options (moduli set, moduli count, profiling events).  With the
+ * defaults it is ti_crt_matmul.  No counterpart in the reference, which has no options:
+ * it extends crt_matmul.py:101 with the opt-in moduli set of the survey's config 2.
+ */
+int ti_crt_matmul_ex(const double *A, int64_t sa0, int64_t sa1, const double *B, int64_t sb0,
+                     int64_t sb1, double *C, int64_t ldc, int64_t m, int64_t n, int64_t k,
+                     int bits, int out_mode, void *workspace, size_t workspace_bytes,
+                     void *stream, const ti_crt_options_t *opt);
 
 /*
  * ti_crt_matmul that also records four caller-created CUDA events (cudaEvent_t, passed as

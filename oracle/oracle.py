@@ -13,6 +13,7 @@ Each wrapper restates one function of the reference module
 ``residue_gemm``       ``_matmul_residues``     crt_matmul.py:55-65
 ``crt_reconstruct``    ``_crt_reconstruct``     crt_matmul.py:68-98
 ``crt_matmul``         ``crt_matmul``           crt_matmul.py:101-126
+``crt_matmul_moduli``  the same with explicit moduli and precision
 =====================  ==============================================
 """
 
@@ -64,6 +65,9 @@ def lib():
         L.or_crt_reconstruct.restype = i32
         L.or_crt_matmul.argtypes = [p, i64, i64, p, i64, i64, i64, i64, i64, i32, p, i64]
         L.or_crt_matmul.restype = i32
+        L.or_crt_matmul_moduli.argtypes = [p, i64, i64, p, i64, i64, i64, i64, i64, p, i32, i32,
+                                           p, i64]
+        L.or_crt_matmul_moduli.restype = i32
         _lib = L
     return _lib
 
@@ -144,3 +148,21 @@ def crt_matmul(A: np.ndarray, B: np.ndarray, bits: int = 53) -> np.ndarray:
 
 def set_threads(n: int) -> None:
     os.environ["OMP_NUM_THREADS"] = str(n)
+
+
+def crt_matmul_moduli(A: np.ndarray, B: np.ndarray, moduli, bits: int) -> np.ndarray:
+    """The reference algorithm with an explicit moduli set (pairwise coprime, < 256) and
+    precision ``bits`` in place of ``_PRIMES[:n]`` and ``_PRECISION_BITS[dtype]``."""
+    A = np.asarray(A, dtype=np.float64)
+    B = np.asarray(B, dtype=np.float64)
+    m, k = A.shape
+    n = B.shape[1]
+    mods = np.asarray(moduli, np.int32)
+    out = np.empty((m, n), np.float64)
+    sa = [s // 8 for s in A.strides]
+    sb = [s // 8 for s in B.strides]
+    rc = lib().or_crt_matmul_moduli(_ptr(A), sa[0], sa[1], _ptr(B), sb[0], sb[1], m, n, k,
+                                    _ptr(mods), len(mods), bits, _ptr(out), n)
+    if rc != 0:
+        raise ValueError(f"oracle failed ({rc})")
+    return out

@@ -13,6 +13,8 @@
  *   or_residue_gemm      src/tensor_inv/crt_matmul.py:55-65   (_matmul_residues, CPU branch)
  *   or_crt_reconstruct   src/tensor_inv/crt_matmul.py:68-98   (_crt_precompute + _crt_reconstruct)
  *   or_crt_matmul        src/tensor_inv/crt_matmul.py:101-126 (crt_matmul, CPU branch)
+ *   or_crt_matmul_moduli the same path with a caller-chosen moduli set and precision
+ *                        (the opt-in wide-moduli scheme; the steps are unchanged)
  *
  * Parity is pinned against fixtures produced by the reference itself
  * (tests/golden/make_golden.py) and checked in tests/test_oracle_golden.py.
@@ -315,6 +317,61 @@ int or_crt_reconstruct(const int32_t *residues, int n_mod, const int32_t *moduli
         }
     }
     return 0;
+}
+
+/* ------------------------------------------------------------------------ */
+/* crt_matmul.py:101-126 with an explicit moduli set and precision: the     */
+/* same four steps (scale + residues, per-modulus int32 GEMM mod m_i,       */
+/* bigint CRT, ldexp) for any pairwise-coprime moduli < 256.  bits is used  */
+/* exactly as the reference uses _PRECISION_BITS[dtype].                    */
+/* Returns 0, -2 on allocation failure, -1 for bad moduli.                  */
+/* ------------------------------------------------------------------------ */
+int or_crt_matmul_moduli(const double *A, int64_t sa0, int64_t sa1, const double *B,
+                         int64_t sb0, int64_t sb1, int64_t m, int64_t n, int64_t k,
+                         const int32_t *moduli, int n_mod, int bits, double *C, int64_t ldc) {
+    if (n_mod < 1 || n_mod > OR_MAX_MODULI) return -1;
+    size_t na = (size_t)n_mod * (size_t)m * (size_t)k, nb = (size_t)n_mod * (size_t)k * (size_t)n;
+    int8_t *ar = (int8_t *)malloc(na ? na : 1);
+    int8_t *br_t = (int8_t *)malloc(nb ? nb : 1);
+    int8_t *br = (int8_t *)malloc(nb ? nb : 1);
+    int32_t *re = (int32_t *)malloc(sizeof(int32_t) * (m ? m : 1));
+    int32_t *ce = (int32_t *)malloc(sizeof(int32_t) * (n ? n : 1));
+    int32_t *cr = (int32_t *)malloc(sizeof(int32_t) * (size_t)n_mod * (size_t)m * (size_t)n + 4);
+    int rc = 0;
+    if (!ar || !br_t || !br || !re || !ce || !cr) {
+        rc = -2;
+        goto done;
+    }
+    /* residues are stored as int8 of the floor-mod value; moduli above 128 keep the same
+       bits in a uint8 view, so the GEMM below reads them back as unsigned */
+    or_split(A, m, k, sa0, sa1, bits, n_mod, moduli, re, ar);
+    or_split(B, n, k, sb1, sb0, bits, n_mod, moduli, ce, br_t);
+    for (int i = 0; i < n_mod; ++i)
+        for (int64_t j = 0; j < n; ++j)
+            for (int64_t l = 0; l < k; ++l)
+                br[((int64_t)i * k + l) * n + j] = br_t[((int64_t)i * n + j) * k + l];
+#pragma omp parallel for collapse(2) schedule(dynamic, 4)
+    for (int i = 0; i < n_mod; ++i) {
+        for (int64_t r = 0; r < m; ++r) {
+            const uint8_t *a = (const uint8_t *)ar + ((int64_t)i * m + r) * k;
+            const uint8_t *b = (const uint8_t *)br + (int64_t)i * k * n;
+            int32_t *acc = cr + ((int64_t)i * m + r) * n;
+            for (int64_t j = 0; j < n; ++j) acc[j] = 0;
+            for (int64_t l = 0; l < k; ++l) {
+                int32_t av = a[l];
+                const uint8_t *brow = b + l * n;
+                /* partial sums stay exact: reduce every 16384 steps (255*255*16384 < 2^31) */
+                for (int64_t j = 0; j < n; ++j) acc[j] += av * (int32_t)brow[j];
+                if ((l & 16383) == 16383)
+                    for (int64_t j = 0; j < n; ++j) acc[j] %= moduli[i];
+            }
+            for (int64_t j = 0; j < n; ++j) acc[j] %= moduli[i];
+        }
+    }
+    rc = or_crt_reconstruct(cr, n_mod, moduli, bits, re, ce, m, n, C, ldc);
+done:
+    free(ar), free(br_t), free(br), free(re), free(ce), free(cr);
+    return rc;
 }
 
 /* ------------------------------------------------------------------------ */

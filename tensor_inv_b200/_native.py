@@ -25,11 +25,24 @@ TI_OUT_STORE = 0
 TI_OUT_SUBTRACT = 1
 TI_OUT_ADD = 2
 
+TI_MODULI_PRIMES = 0
+TI_MODULI_WIDE = 1
+
 TI_NONFINITE_EXP = -(2**31)
 TI_MAX_K = 135263
 
 # name -> (restype, argtypes); mirrors include/tensor_inv_crt.h
 _i64, _int, _p, _sz = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t
+
+
+class CrtOptions(ctypes.Structure):
+    """ti_crt_options_t."""
+
+    _fields_ = [("moduli", ctypes.c_int), ("n_moduli", ctypes.c_int),
+                ("stage_events", ctypes.c_void_p * 4)]
+
+
+_opt = ctypes.POINTER(CrtOptions)
 SIGNATURES = {
     "ti_status_string": (ctypes.c_char_p, [_int]),
     "ti_version": (ctypes.c_char_p, []),
@@ -46,6 +59,11 @@ SIGNATURES = {
                                     _int, _int, _p, _sz, _p, _p]),
     "ti_crt_matmul_noalloc": (_int, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i64,
                                      _i64, _int, _int, _p]),
+    "ti_crt_plan": (_int, [_i64, _int, _opt, ctypes.POINTER(_int), ctypes.POINTER(_int),
+                           ctypes.POINTER(ctypes.c_int32)]),
+    "ti_crt_workspace_size_ex": (_int, [_i64, _i64, _i64, _int, _opt, ctypes.POINTER(_sz)]),
+    "ti_crt_matmul_ex": (_int, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i64, _i64, _int,
+                                _int, _p, _sz, _p, _opt]),
     "ti_device_error": (_int, [ctypes.POINTER(_int), _int]),
 }
 
@@ -102,6 +120,46 @@ def primes() -> list[int]:
 def crt_workspace_size(m: int, n: int, k: int, bits: int) -> int:
     out = ctypes.c_size_t(0)
     check("ti_crt_workspace_size", lib().ti_crt_workspace_size(m, n, k, bits, ctypes.byref(out)))
+    return out.value
+
+
+def options(moduli=None, n_moduli=None, events=None) -> CrtOptions:
+    """ti_crt_options_t from Python values: moduli None/'primes' or 'wide'."""
+    if moduli in (None, "primes"):
+        kind = TI_MODULI_PRIMES
+    elif moduli == "wide":
+        kind = TI_MODULI_WIDE
+    else:
+        raise ValueError(f"moduli must be None, 'primes' or 'wide', got {moduli!r}")
+    n = 0 if n_moduli is None else int(n_moduli)
+    if n < 0:
+        raise ValueError("n_moduli must be positive")
+    o = CrtOptions(kind, n)
+    if events is not None:
+        for i, e in enumerate(events):
+            o.stage_events[i] = e
+    return o
+
+
+def crt_plan(k: int, bits: int, moduli=None, n_moduli=None):
+    """(n_moduli, bits kept, moduli list) that ti_crt_matmul_ex uses for inner dimension k."""
+    o = options(moduli, n_moduli)
+    n = ctypes.c_int(0)
+    b = ctypes.c_int(0)
+    mods = (ctypes.c_int32 * 32)()
+    st = lib().ti_crt_plan(int(k), int(bits), ctypes.byref(o), ctypes.byref(n), ctypes.byref(b),
+                           mods)
+    if st == TI_ERR_UNSUPPORTED:
+        raise ValueError(f"no moduli plan for inner dim {k}, bits {bits}, moduli {moduli!r}, "
+                         f"n_moduli {n_moduli!r}")
+    check("ti_crt_plan", st)
+    return n.value, b.value, [int(mods[i]) for i in range(n.value)]
+
+
+def crt_workspace_size_ex(m: int, n: int, k: int, bits: int, opt: CrtOptions) -> int:
+    out = ctypes.c_size_t(0)
+    check("ti_crt_workspace_size_ex",
+          lib().ti_crt_workspace_size_ex(m, n, k, bits, ctypes.byref(opt), ctypes.byref(out)))
     return out.value
 
 

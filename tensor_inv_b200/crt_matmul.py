@@ -88,9 +88,9 @@ def _check_dtype(A):
     return bits
 
 
-def _launch_crt_matmul(A, B, C, bits, out_mode):
+def _launch_crt_matmul(A, B, C, bits, out_mode, opt=None):
     """C (op)= A @ B on the device of C; A, B float64 on the same device, C float64 with
-    unit column stride.  Returns C."""
+    unit column stride; ``opt`` a ti_crt_options_t (None: the reference's moduli).  Returns C."""
     m, k = A.shape
     n = B.shape[1]
     dev = C.device
@@ -105,21 +105,38 @@ def _launch_crt_matmul(A, B, C, bits, out_mode):
     if C.stride(1) != 1 and n > 1:
         raise ValueError("output must have unit column stride")
     ldc = C.stride(0) if m > 1 else max(n, 1)
-    ws_bytes = nat.crt_workspace_size(m, n, k, bits)
+    if opt is None:
+        opt = nat.options()
+    ws_bytes = nat.crt_workspace_size_ex(m, n, k, bits, opt)
     ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
     with torch.cuda.device(dev):
-        st = nat.lib().ti_crt_matmul(
+        st = nat.lib().ti_crt_matmul_ex(
             A.data_ptr(), sa[0], sa[1], B.data_ptr(), sb[0], sb[1], C.data_ptr(), ldc, m, n,
-            k, bits, out_mode, ws.data_ptr(), ws.numel(), _stream_ptr(dev))
-    nat.check("ti_crt_matmul", st)
+            k, bits, out_mode, ws.data_ptr(), ws.numel(), _stream_ptr(dev), ctypes.byref(opt))
+    nat.check("ti_crt_matmul_ex", st)
     return C
 
 
-def crt_matmul(A, B):
+def _options(k, bits, moduli, n_moduli):
+    """Validated ti_crt_options_t; raises ValueError like _n_moduli when no plan exists."""
+    if moduli in (None, "primes") and n_moduli is None:
+        _n_moduli(k, bits)  # the reference's ValueError, unchanged
+    nat.crt_plan(k, bits, moduli, n_moduli)
+    return nat.options(moduli, n_moduli)
+
+
+def crt_matmul(A, B, *, moduli=None, n_moduli=None):
     """FP-accurate matmul via int8 CRT. Precision matches input dtype.
 
     Same contract as the reference (crt_matmul.py:101-126): ``bits`` from ``A.dtype``,
     operands promoted to float64, result float64 on ``A``'s device.
+
+    Keyword-only extensions (absent from the reference; the defaults are its scheme):
+    ``moduli='wide'`` uses pairwise-coprime odd moduli up to 255 instead of the primes up
+    to 127; with ``n_moduli=None`` it takes the fewest that keep every bit of the input
+    precision, so the result is bit-identical with about a third fewer residue GEMMs.
+    ``n_moduli=N`` fixes the count (the survey's config-2 sweep); if N moduli cannot hold
+    the full precision, the scaling keeps the largest b with prod(moduli) > 2*k*2^(2b) bits.
     """
     bits = _check_dtype(A)
     if A.dim() != 2 or B.dim() != 2:
@@ -131,8 +148,7 @@ def crt_matmul(A, B):
     if B.shape[0] != k:
         raise RuntimeError(f"crt_matmul: shapes {tuple(A.shape)} and {tuple(B.shape)} "
                            "cannot be multiplied")
-    n_mod = _n_moduli(k, bits)  # ValueError as in the reference
-    del n_mod
+    opt = _options(k, bits, moduli, n_moduli)  # ValueError as in the reference
     n = B.shape[1]
     home = A.device
     dev = _cuda_device(A, B)
@@ -140,7 +156,7 @@ def crt_matmul(A, B):
     B = B.to(device=dev, dtype=torch.float64)
     C = torch.empty((m, n), dtype=torch.float64, device=dev)
     if m and n:
-        _launch_crt_matmul(A, B, C, bits, nat.TI_OUT_STORE)
+        _launch_crt_matmul(A, B, C, bits, nat.TI_OUT_STORE, opt)
     if home == dev:
         return C
     if home.type == "cpu":
@@ -151,7 +167,7 @@ def crt_matmul(A, B):
     return C.to(home)
 
 
-def crt_matmul_update(C, A, B, alpha=-1):
+def crt_matmul_update(C, A, B, alpha=-1, *, moduli=None, n_moduli=None):
     """In-place ``C += alpha * crt_matmul(A, B)`` for alpha in {-1, +1}, C float64 CUDA.
 
     Bit-identical to ``C -= crt_matmul(A, B)`` (alpha=-1) or ``C += crt_matmul(A, B)``:
@@ -168,11 +184,11 @@ def crt_matmul_update(C, A, B, alpha=-1):
         raise RuntimeError("crt_matmul_update: shape mismatch")
     if m == 0 or B.shape[1] == 0 or k == 0:
         return C
-    _n_moduli(k, bits)
+    opt = _options(k, bits, moduli, n_moduli)
     A = A.to(device=C.device, dtype=torch.float64)
     B = B.to(device=C.device, dtype=torch.float64)
     return _launch_crt_matmul(A, B, C, bits,
-                              nat.TI_OUT_SUBTRACT if alpha == -1 else nat.TI_OUT_ADD)
+                              nat.TI_OUT_SUBTRACT if alpha == -1 else nat.TI_OUT_ADD, opt)
 
 
 # ---------------------------------------------------------------------------------------

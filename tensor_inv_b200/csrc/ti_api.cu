@@ -3,9 +3,10 @@
 // Host-side planning for the CRT matmul: the modulus count (crt_matmul.py:26 _n_moduli),
 // the per-modulus constants every kernel receives by value, the workspace layout, and the
 // stage sequence K1 (split) -> K2 (tcgen05 residue GEMM) -> K3 (exact CRT).
+#include <cstdlib>
 #include <cstring>
 
-#include "../../include/tensor_inv_crt.h"
+#include "tensor_inv_crt.h"
 #include "ti_common.cuh"
 
 namespace ti {
@@ -20,12 +21,44 @@ cudaError_t launch_crt(const void *R, bool in_u8, int64_t ldr, int64_t plane, in
                        int64_t cols, const int32_t *row_exp, const int32_t *col_exp, double *C,
                        int64_t ldc, int out_mode, const CrtConst &K, int num_sms,
                        cudaStream_t stream);
+int64_t gemm_output_tiles(int64_t m, int64_t n);
+size_t fused_scratch_bytes(int n_mod, int num_ctas);
+cudaError_t launch_fused_gemm_crt(const int8_t *a_res, const int8_t *b_res, int64_t m, int64_t n,
+                                  int64_t kdim, int64_t ld, const CrtConst &K,
+                                  const int32_t *row_exp, const int32_t *col_exp, double *C,
+                                  int64_t ldc, int out_mode, uint8_t *scratch, int grid, int *err,
+                                  cudaStream_t stream);
+
+// The fused GEMM+CRT kernel (K2+K3 in one launch) is opt-in (TI_CRT_PATH=fused): measured
+// on B200 at 8192^3 its tile-major order (all moduli of one tile back to back) costs the
+// GEMM ~20% in L2 reuse, more than the separate reconstruction kernel it hides.
+// Scratch of the fused kernel is sized for at most this many CTAs (one per SM).
+constexpr int kFusedMaxCtas = 192;
+
+// TI_CRT_PATH=fused selects the fused kernel (default: K2 then K3), for tests and tuning.
+// Read on every call so one process can exercise both paths.
+static int path_override() {
+    const char *e = getenv("TI_CRT_PATH");
+    return (e && !strcmp(e, "fused")) ? 1 : (e && !strcmp(e, "unfused")) ? 0 : -1;
+}
+
+static bool use_fused(int64_t m, int64_t n) {
+    return path_override() == 1 && gemm_output_tiles(m, n) >= 1;
+}
 
 // The device error word: kernels record a bounded wait that ran out here.
 __device__ int g_device_error = 0;
 
 static const int32_t kPrimes[30] = {3,  5,  7,  11, 13, 17, 19, 23, 29,  31,  37,  41,  43,  47,  53,
                                     59, 61, 67, 71, 73, 79, 83, 89, 97, 101, 103, 107, 109, 113, 127};
+// Pairwise-coprime odd moduli up to 255, largest first (each taken greedily when coprime
+// with all larger ones).  Sixteen of them multiply to 2^124.95.
+static const int32_t kWide[16] = {255, 253, 251, 247, 241, 239, 233, 229,
+                                  227, 223, 217, 211, 199, 197, 193, 191};
+constexpr int kMaxPrimesModuli = 25;  // prod(first 25 primes) = 2^126.5 < 2^127
+constexpr int kMaxWideModuli = 16;    // prod(16 wide moduli) = 2^124.95 < 2^127
+// |symmetric residue| <= 127 for the wide moduli: 127*127*k < 2^31 - 256
+constexpr int64_t kMaxKWide = 133144;
 
 typedef unsigned __int128 u128;
 
@@ -68,6 +101,57 @@ static int n_moduli_exact(int64_t k, int bits) {
 }
 
 // ---------------------------------------------------------------------------------------
+// moduli plan: which moduli, how many, and the precision kept
+// ---------------------------------------------------------------------------------------
+struct Plan {
+    int n_mod;
+    int bits;        // precision actually kept (<= the requested bits)
+    bool wide;
+    int32_t moduli[kMaxModuli];
+};
+
+// Largest b <= bits with prod(moduli[:n]) > 2*k*2^(2b), or 0 if none.  Exact (u128).
+static int bits_for(const int32_t *moduli, int n, int64_t k, int bits) {
+    u128 M = 1;
+    for (int i = 0; i < n; ++i) M *= static_cast<uint32_t>(moduli[i]);
+    for (int b = bits; b >= 1; --b)
+        if ((static_cast<u128>(static_cast<uint64_t>(k)) << (2 * b + 1)) < M) return b;
+    return 0;
+}
+
+static int make_plan(int64_t k, int bits, const ti_crt_options_t *opt, Plan &P) {
+    const int kind = opt ? opt->moduli : TI_MODULI_PRIMES;
+    const int want = opt ? opt->n_moduli : 0;
+    if (kind != TI_MODULI_PRIMES && kind != TI_MODULI_WIDE) return TI_ERR_INVALID_ARGUMENT;
+    if (want < 0) return TI_ERR_INVALID_ARGUMENT;
+    P.wide = kind == TI_MODULI_WIDE;
+    const int32_t *set = P.wide ? kWide : kPrimes;
+    const int max_n = P.wide ? kMaxWideModuli : kMaxPrimesModuli;
+    if (k > (P.wide ? kMaxKWide : int64_t(TI_MAX_K))) return TI_ERR_UNSUPPORTED;
+    if (want > max_n) return TI_ERR_UNSUPPORTED;
+    if (want == 0 && !P.wide) {
+        P.n_mod = n_moduli_exact(k, bits);  // crt_matmul.py:26-35
+        P.bits = bits;
+        if (P.n_mod < 0 || P.n_mod > max_n) return TI_ERR_UNSUPPORTED;
+    } else if (want == 0) {
+        P.n_mod = -1;
+        for (int n = 1; n <= max_n; ++n)
+            if (bits_for(set, n, k, bits) == bits) {
+                P.n_mod = n;
+                break;
+            }
+        if (P.n_mod < 0) return TI_ERR_UNSUPPORTED;
+        P.bits = bits;
+    } else {
+        P.n_mod = want;
+        P.bits = bits_for(set, want, k, bits);
+        if (P.bits < 1) return TI_ERR_UNSUPPORTED;
+    }
+    for (int i = 0; i < P.n_mod; ++i) P.moduli[i] = set[i];
+    return TI_OK;
+}
+
+// ---------------------------------------------------------------------------------------
 // per-modulus constants
 // ---------------------------------------------------------------------------------------
 static bool is_pow2(uint32_t x) { return (x & (x - 1)) == 0; }
@@ -88,17 +172,20 @@ static bool make_magic(const int32_t *moduli, int n, ModMagic &mm) {
         u128 mg = (num + p - 1) / p;
         if (is_pow2(p)) mg = (static_cast<u128>(1) << 32) - 1;  // unused (uint8 path is odd p)
         mm.magic[i] = static_cast<uint32_t>(mg);
+        mm.off[i] = p * (((uint32_t(1) << 31) + p - 1) / p);
     }
     return true;
 }
 
-static bool make_split_const(int n_mod, int bits, SplitConst &C) {
+static bool make_split_const(const int32_t *moduli, int n_mod, int bits, bool symmetric,
+                             SplitConst &C) {
     std::memset(&C, 0, sizeof(C));
     C.n_mod = n_mod;
     C.bits = bits;
-    if (!make_magic(kPrimes, n_mod, C.mm)) return false;
+    C.symmetric = symmetric ? 1 : 0;
+    if (!make_magic(moduli, n_mod, C.mm)) return false;
     for (int i = 0; i < n_mod; ++i) {
-        const uint64_t p = kPrimes[i];
+        const uint64_t p = static_cast<uint32_t>(moduli[i]);
         C.w32[i] = static_cast<uint32_t>((uint64_t(1) << 32) % p);
         C.w16[i] = static_cast<uint32_t>((uint64_t(1) << 16) % p);
         C.bigp[i] = static_cast<uint32_t>(p * (((uint64_t(1) << 29) + p - 1) / p));
@@ -241,19 +328,22 @@ int ti_n_moduli(int64_t k, int bits, int *n_out) {
 
 // Workspace layout of ti_crt_matmul (each piece 256-byte aligned):
 //   row_exp int32[m] | col_exp int32[n] | A residues int8[N][m][ldk] |
-//   B residues int8[N][n][ldk] | product residues uint8[N][m][ldr]
+//   B residues int8[N][n][ldk] | product residues uint8[N][m][ldr] (K2 then K3)
+//                                or per-CTA slots uint8[CTAs][2][N][128][256] (fused)
 struct CrtLayout {
     int n_mod;
+    Plan plan;
     int64_t ldk, ldr;
     size_t off_rexp, off_cexp, off_a, off_b, off_r, total;
 };
 
-static int crt_layout(int64_t m, int64_t n, int64_t k, int bits, CrtLayout &L) {
+static int crt_layout(int64_t m, int64_t n, int64_t k, int bits, const ti_crt_options_t *opt,
+                      CrtLayout &L) {
     if (m < 0 || n < 0 || k < 0) return TI_ERR_INVALID_ARGUMENT;
     if (bits != 8 && bits != 11 && bits != 24 && bits != 53) return TI_ERR_INVALID_ARGUMENT;
-    if (k > TI_MAX_K) return TI_ERR_UNSUPPORTED;
-    L.n_mod = n_moduli_exact(k, bits);
-    if (L.n_mod < 0 || L.n_mod > kMaxModuli) return TI_ERR_UNSUPPORTED;
+    const int rc = make_plan(k, bits, opt, L.plan);
+    if (rc != TI_OK) return rc;
+    L.n_mod = L.plan.n_mod;
     L.ldk = round_up(k > 0 ? k : 1, 16);
     L.ldr = round_up(n > 0 ? n : 1, 16);
     size_t off = 0;
@@ -261,17 +351,38 @@ static int crt_layout(int64_t m, int64_t n, int64_t k, int bits, CrtLayout &L) {
     L.off_cexp = off; off += align256(sizeof(int32_t) * size_t(n));
     L.off_a = off; off += align256(size_t(L.n_mod) * size_t(m) * size_t(L.ldk));
     L.off_b = off; off += align256(size_t(L.n_mod) * size_t(n) * size_t(L.ldk));
-    L.off_r = off; off += align256(size_t(L.n_mod) * size_t(m) * size_t(L.ldr));
+    L.off_r = off;
+    const size_t planes = align256(size_t(L.n_mod) * size_t(m) * size_t(L.ldr));
+    const size_t slots = align256(fused_scratch_bytes(L.n_mod, kFusedMaxCtas));
+    off += use_fused(m, n) ? slots : planes;
     L.total = off;
     return TI_OK;
 }
 
-int ti_crt_workspace_size(int64_t m, int64_t n, int64_t k, int bits, size_t *bytes) {
+int ti_crt_workspace_size_ex(int64_t m, int64_t n, int64_t k, int bits,
+                             const ti_crt_options_t *opt, size_t *bytes) {
     if (!bytes) return TI_ERR_INVALID_ARGUMENT;
     CrtLayout L;
-    const int rc = crt_layout(m, n, k, bits, L);
+    const int rc = crt_layout(m, n, k, bits, opt, L);
     if (rc != TI_OK) return rc;
     *bytes = L.total;
+    return TI_OK;
+}
+
+int ti_crt_workspace_size(int64_t m, int64_t n, int64_t k, int bits, size_t *bytes) {
+    return ti_crt_workspace_size_ex(m, n, k, bits, nullptr, bytes);
+}
+
+int ti_crt_plan(int64_t k, int bits, const ti_crt_options_t *opt, int *n_mod_out,
+                int *bits_eff_out, int32_t *moduli_out) {
+    if (k < 0 || bits < 1 || bits > 53) return TI_ERR_INVALID_ARGUMENT;
+    Plan P;
+    const int rc = make_plan(k, bits, opt, P);
+    if (rc != TI_OK) return rc;
+    if (n_mod_out) *n_mod_out = P.n_mod;
+    if (bits_eff_out) *bits_eff_out = P.bits;
+    if (moduli_out)
+        for (int i = 0; i < P.n_mod; ++i) moduli_out[i] = P.moduli[i];
     return TI_OK;
 }
 
@@ -289,7 +400,7 @@ int ti_crt_split(const double *X, int64_t outer, int64_t kdim, int64_t s_outer, 
     int rc = device_info(d);
     if (rc != TI_OK) return rc;
     SplitConst C;
-    if (!make_split_const(n_mod, bits, C)) return TI_ERR_INVALID_ARGUMENT;
+    if (!make_split_const(kPrimes, n_mod, bits, false, C)) return TI_ERR_INVALID_ARGUMENT;
     // s_k == 1 selects the k-contiguous kernels (also for a 1-long outer stride)
     const int64_t sk = (s_k == 1) ? 1 : s_k;
     const int64_t so = (s_k == 1) ? s_outer : 1;
@@ -367,17 +478,29 @@ int ti_crt_matmul(const double *A, int64_t sa0, int64_t sa1, const double *B, in
                   int64_t sb1, double *C, int64_t ldc, int64_t m, int64_t n, int64_t k,
                   int bits, int out_mode, void *workspace, size_t workspace_bytes,
                   void *stream) {
-    return ti_crt_matmul_events(A, sa0, sa1, B, sb0, sb1, C, ldc, m, n, k, bits, out_mode,
-                                workspace, workspace_bytes, stream, nullptr);
+    return ti_crt_matmul_ex(A, sa0, sa1, B, sb0, sb1, C, ldc, m, n, k, bits, out_mode,
+                            workspace, workspace_bytes, stream, nullptr);
 }
 
 int ti_crt_matmul_events(const double *A, int64_t sa0, int64_t sa1, const double *B,
                          int64_t sb0, int64_t sb1, double *C, int64_t ldc, int64_t m, int64_t n,
                          int64_t k, int bits, int out_mode, void *workspace,
                          size_t workspace_bytes, void *stream, void *const *ev) {
+    ti_crt_options_t o;
+    std::memset(&o, 0, sizeof(o));
+    for (int i = 0; i < 4 && ev; ++i) o.stage_events[i] = ev[i];
+    return ti_crt_matmul_ex(A, sa0, sa1, B, sb0, sb1, C, ldc, m, n, k, bits, out_mode,
+                            workspace, workspace_bytes, stream, &o);
+}
+
+int ti_crt_matmul_ex(const double *A, int64_t sa0, int64_t sa1, const double *B, int64_t sb0,
+                     int64_t sb1, double *C, int64_t ldc, int64_t m, int64_t n, int64_t k,
+                     int bits, int out_mode, void *workspace, size_t workspace_bytes,
+                     void *stream, const ti_crt_options_t *opt) {
     if (out_mode < TI_OUT_STORE || out_mode > TI_OUT_ADD) return TI_ERR_INVALID_ARGUMENT;
+    void *const *ev = opt ? opt->stage_events : nullptr;
     CrtLayout L;
-    int rc = crt_layout(m, n, k, bits, L);
+    int rc = crt_layout(m, n, k, bits, opt, L);
     if (rc != TI_OK) return rc;
     if (m == 0 || n == 0) return TI_OK;
     if (!C || ldc < n) return TI_ERR_INVALID_ARGUMENT;
@@ -402,8 +525,9 @@ int ti_crt_matmul_events(const double *A, int64_t sa0, int64_t sa1, const double
 
     SplitConst SC;
     CrtConst KC;
-    if (!make_split_const(L.n_mod, bits, SC)) return TI_ERR_UNSUPPORTED;
-    if (!make_crt_const(kPrimes, L.n_mod, bits, KC)) return TI_ERR_UNSUPPORTED;
+    const Plan &PL = L.plan;
+    if (!make_split_const(PL.moduli, PL.n_mod, PL.bits, PL.wide, SC)) return TI_ERR_UNSUPPORTED;
+    if (!make_crt_const(PL.moduli, PL.n_mod, PL.bits, KC)) return TI_ERR_UNSUPPORTED;
 
     // K1: A as m vectors along k (rows), B as n vectors along k (columns)
     cudaError_t e;
@@ -414,8 +538,20 @@ int ti_crt_matmul_events(const double *A, int64_t sa0, int64_t sa1, const double
     if (sb0 == 1) e = launch_split(B, n, k, sb1, 1, SC, cexp, bres, L.ldk, d.num_sms, s);
     else e = launch_split(B, n, k, 1, sb0, SC, cexp, bres, L.ldk, d.num_sms, s);
     if (e != cudaSuccess) return TI_ERR_CUDA;
-    // K2: per-modulus residue GEMMs, mod-reduced to uint8 planes
     record(ev, 1, s);
+    if (use_fused(m, n)) {
+        // K2+K3 fused: residue GEMMs with the CRT of each finished tile in the same kernel
+        int64_t grid = gemm_output_tiles(m, n);
+        if (grid > d.num_sms) grid = d.num_sms;
+        if (grid > kFusedMaxCtas) grid = kFusedMaxCtas;
+        e = launch_fused_gemm_crt(ares, bres, m, n, k, L.ldk, KC, rexp, cexp, C, ldc, out_mode, R,
+                                  static_cast<int>(grid), d.err, s);
+        record(ev, 2, s);
+        record(ev, 3, s);
+        if (e != cudaSuccess) return e == cudaErrorInvalidValue ? TI_ERR_NO_DEVICE : TI_ERR_CUDA;
+        return TI_OK;
+    }
+    // K2: per-modulus residue GEMMs, mod-reduced to uint8 planes
     e = launch_residue_gemm(ares, bres, m, n, k, L.ldk, L.n_mod, SC.mm, R, L.ldr, 0, d.err,
                             d.num_sms, s);
     if (e != cudaSuccess) return e == cudaErrorInvalidValue ? TI_ERR_NO_DEVICE : TI_ERR_CUDA;

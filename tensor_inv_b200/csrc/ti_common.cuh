@@ -33,6 +33,7 @@ struct ModMagic {
     uint32_t p[kMaxModuli];
     uint32_t magic[kMaxModuli];
     uint32_t shift[kMaxModuli];
+    uint32_t off[kMaxModuli];  // p * ceil(2^31 / p): lifts a signed accumulator to [0, 2^32)
 };
 
 __device__ __forceinline__ uint32_t mod_small(uint32_t a, uint32_t p, uint32_t magic,
@@ -41,10 +42,22 @@ __device__ __forceinline__ uint32_t mod_small(uint32_t a, uint32_t p, uint32_t m
     return a - q * p;
 }
 
+// acc mod p in [0, p) for a signed int32 accumulator with |acc| <= 2^31 - 256 (passed as
+// its bit pattern).  a = acc + off lies in [0, 2^32); for such a the quotient estimate
+// above is at most one too large (error below 2^-shift < 2/p), fixed by one add.
+__device__ __forceinline__ uint32_t mod_acc(uint32_t acc, uint32_t p, uint32_t magic,
+                                            uint32_t shift, uint32_t off) {
+    const uint32_t a = acc + off;
+    const int32_t r = static_cast<int32_t>(a - (__umulhi(a, magic) >> shift) * p);
+    return static_cast<uint32_t>(r < 0 ? r + static_cast<int32_t>(p) : r);
+}
+
 // Constants of the split (scale + residue) kernels.
 struct SplitConst {
     int n_mod;
     int bits;
+    int symmetric;  // 0: floor-mod residues in [0, p) (the reference's _residues);
+                    // 1: symmetric residues in [-(p-1)/2, (p-1)/2] (moduli up to 255)
     ModMagic mm;
     uint32_t w32[kMaxModuli];   // 2^32 mod p
     uint32_t w16[kMaxModuli];   // 2^16 mod p

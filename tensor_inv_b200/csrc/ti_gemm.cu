@@ -1,51 +1,72 @@
-// ti_gemm.cu -- K2: the per-modulus residue GEMMs as one persistent tcgen05 kernel.
+// ti_gemm.cu -- K2: the per-modulus residue GEMMs as one persistent tcgen05 kernel, with an
+// optional fused CRT stage (K2+K3).
 //
-// Restates src/tensor_inv/csrc/crt_kernel.cu:17-91 (cuBLASLt batched int8 GEMM followed
-// by the mod_reduce kernel, crt_kernel.cu:6-15) as a single sm_100a kernel:
+// Restates src/tensor_inv/csrc/crt_kernel.cu:17-91 (cuBLASLt batched int8 GEMM followed by
+// the mod_reduce kernel, crt_kernel.cu:6-15):
 //   R[i] = (A_i @ B_i^T) mod p_i   for every modulus i,
 // with A_i (rows x K) and B_i (cols x K) int8 residue planes stored K-major.
 //
-// Design (one CTA per SM, persistent over (modulus, tile_m, tile_n) work units):
+// Roles (one CTA per SM, persistent):
 //   warp 0      TMA producer: 128x128-byte A tile + 256x128-byte B tile per stage,
 //               4-stage mbarrier ring, 128-byte swizzle, no multicast.
-//   warp 1      TMEM allocator + single-thread tcgen05.mma.kind::i8 issuer,
-//               M=128 N=256 K=32 per instruction, int32 accumulators in TMEM,
-//               double-buffered (2 x 256 columns = all 512 TMEM columns).
-//   warps 2..5  epilogue: tcgen05.ld 32 rows x 32 columns at a time, exact mod p, pack,
-//               store.  The epilogue of tile t overlaps the main loop of tile t+1.
+//   warp 1      TMEM allocator + single-thread tcgen05.mma.kind::i8 issuer, M=128 N=256
+//               K=32 per instruction, int32 accumulators in TMEM, double-buffered
+//               (2 x 256 columns = all 512 TMEM columns).
+//   warps 2..5  epilogue: tcgen05.ld 32 rows x 32 columns at a time, exact mod p, pack.
+//   warps 6..9  (fused mode only) CRT: exact reconstruction of a finished output tile.
+//
+// Unfused mode: work units are (modulus, tile) in modulus-major order; the epilogue writes
+// uint8 residue planes R[i][m][ldo] (or int32 planes) that K3 (ti_crt.cu) consumes.
+// Fused mode: each CTA takes whole 128x256 output tiles and runs all N moduli of a tile
+// back to back.  The epilogue stores t_i = (r_i * u_i) mod p_i for every modulus into one
+// of two per-CTA scratch slots ([N][128][256] bytes); after the last modulus the CRT warps
+// rebuild the float64 tile from that slot while the tensor cores move on to the next tile,
+// so the reconstruction hides behind the MMA.
+//
 // Every wait is bounded; on timeout the CTA raises an error word, drains its in-flight
 // copies and MMAs, frees TMEM and exits.
-#include "ti_common.cuh"
+#include <cstring>
+
+#include "ti_crt_math.cuh"
 
 namespace ti {
 
 constexpr int kBM = 128, kBN = 256, kBK = 128, kStages = 4;
 constexpr int kABytes = kBM * kBK, kBBytes = kBN * kBK, kStageBytes = kABytes + kBBytes;
-constexpr int kGemmThreads = 192;
+constexpr int kEpiThreads = 128, kCrtThreads = 128;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kIdesc = make_idesc_i8(kBM, kBN);
 constexpr int kGroupM = 16;  // tile raster: 16 row-tiles per group for L2 reuse
 constexpr size_t kGemmSmemBytes = size_t(kStages) * kStageBytes + 1024 /*align*/ + 256 /*bars*/;
+constexpr int64_t kSlotPlaneBytes = int64_t(kBM) * kBN;  // one modulus of one tile, uint8
+
+__host__ __device__ constexpr int gemm_threads(bool fused) {
+    return 64 + kEpiThreads + (fused ? kCrtThreads : 0);
+}
 
 struct GemmParams {
     int64_t m, n;      // output rows / columns per modulus
     int num_kb;        // K blocks of 128 bytes
     int n_mod;
     int tiles_m, tiles_n;
-    int64_t total_tiles;
+    int64_t total_units;  // n_mod * tiles_m * tiles_n
+    // unfused output
     void *out;         // uint8 [n_mod][m][ldo] or int32 [n_mod][m][ldo]
     int64_t ldo;       // elements; multiple of 16 for uint8 output
     int64_t plane;     // elements between moduli planes
-    int out_i32;       // 0: uint8 residues (inputs in [0, p)); 1: int32, any int8 inputs
+    int out_i32;       // 0: uint8 residues (|accumulator| <= 2^31 - 256); 1: int32, any int8
+    // fused output
+    uint8_t *scratch;  // 2 slots x n_mod x 128 x 256 bytes per CTA
+    const int32_t *row_exp, *col_exp;
+    double *C;
+    int64_t ldc;
+    int out_mode;      // 0 store, 1 subtract, 2 add
     ModMagic mm;
+    CrtConst crt;      // fused mode: reconstruction constants (crt.u also used by epilogue)
     int *err;
 };
 
-__device__ __forceinline__ void decode_tile(const GemmParams &P, int64_t t, int &mod, int &tm,
-                                            int &tn) {
-    const int64_t per_mod = int64_t(P.tiles_m) * P.tiles_n;
-    mod = static_cast<int>(t / per_mod);
-    const int64_t r = t - int64_t(mod) * per_mod;
+__device__ __forceinline__ void decode_tile(const GemmParams &P, int64_t r, int &tm, int &tn) {
     const int64_t per_group = int64_t(kGroupM) * P.tiles_n;
     const int g = static_cast<int>(r / per_group);
     const int first_m = g * kGroupM;
@@ -55,12 +76,99 @@ __device__ __forceinline__ void decode_tile(const GemmParams &P, int64_t t, int 
     tn = static_cast<int>(rg / gsize);
 }
 
+// Work-unit order seen by every role of one CTA.  Unfused: units strided over the grid in
+// modulus-major order.  Fused: output tiles strided over the grid, all moduli of a tile
+// consecutively.  f(mod, tm, tn, tile_local) returns false to stop.
+template <bool kFused, class F>
+__device__ __forceinline__ void for_each_unit(const GemmParams &P, F &&f) {
+    if (!kFused) {
+        const int64_t per_mod = int64_t(P.tiles_m) * P.tiles_n;
+        for (int64_t u = blockIdx.x; u < P.total_units; u += gridDim.x) {
+            const int mod = static_cast<int>(u / per_mod);
+            int tm, tn;
+            decode_tile(P, u - int64_t(mod) * per_mod, tm, tn);
+            if (!f(mod, tm, tn, int64_t(0))) return;
+        }
+    } else {
+        const int64_t tiles = int64_t(P.tiles_m) * P.tiles_n;
+        int64_t local = 0;
+        for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
+            int tm, tn;
+            decode_tile(P, t, tm, tn);
+            for (int mod = 0; mod < P.n_mod; ++mod)
+                if (!f(mod, tm, tn, local)) return;
+        }
+    }
+}
+
 __device__ __forceinline__ void raise_error(const GemmParams &P, volatile int *abort, int code) {
     *abort = 1;
     atomicCAS(P.err, 0, code);
 }
 
-__global__ void __launch_bounds__(kGemmThreads, 1)
+// CRT of one finished 128 x 256 tile from scratch slot `slot` ([n_mod][128][256] bytes of t_i).
+// CRT thread ct (0..127): warp w = ct / 32 takes rows w, w+4, ...; lane l takes 4 columns.
+__device__ __forceinline__ void crt_tile(const GemmParams &P, const uint8_t *slot, int tm, int tn,
+                                         int ct) {
+    const int w = ct >> 5, lane = ct & 31;
+    const CrtConst &K = P.crt;
+    const bool vec_out = ((reinterpret_cast<uintptr_t>(P.C) & 15) == 0) && ((P.ldc & 1) == 0);
+#pragma unroll 1
+    for (int it = w; it < kBM * 2; it += 4) {
+        const int r = it >> 1, half = it & 1;
+        const int64_t row = int64_t(tm) * kBM + r;
+        if (row >= P.m) continue;  // warp-uniform
+        const int cl = half * 128 + lane * 4;
+        const int64_t col = int64_t(tn) * kBN + cl;
+        if (col >= P.n) continue;
+        const uint8_t *src = slot + r * kBN + cl;
+        // all moduli's residue words in flight at once (the slot is read once, from L2)
+        uint32_t w4[kMaxModuli];
+#pragma unroll
+        for (int i = 0; i < kMaxModuli; ++i)
+            w4[i] = i < K.n_mod ? __ldcg(reinterpret_cast<const unsigned int *>(src + i * kSlotPlaneBytes))
+                                : 0u;
+        uint64_t s0[4] = {0, 0, 0, 0}, s1[4] = {0, 0, 0, 0}, s2[4] = {0, 0, 0, 0},
+                 s3[4] = {0, 0, 0, 0}, f[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int i = 0; i < kMaxModuli; ++i) {
+            if (i >= K.n_mod) break;
+            const uint32_t m0 = K.Mi[i][0], m1 = K.Mi[i][1], m2 = K.Mi[i][2], m3 = K.Mi[i][3];
+            const uint32_t fi = K.finv[i];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const uint32_t t = (w4[i] >> (8 * e)) & 0xFFu;
+                s0[e] += static_cast<uint64_t>(t) * m0;
+                s1[e] += static_cast<uint64_t>(t) * m1;
+                s2[e] += static_cast<uint64_t>(t) * m2;
+                s3[e] += static_cast<uint64_t>(t) * m3;
+                f[e] += static_cast<uint64_t>(t) * fi;
+            }
+        }
+        const int re = P.row_exp[row];
+        const int nc = P.n - col < 4 ? static_cast<int>(P.n - col) : 4;
+        double outv[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int ce = e < nc ? P.col_exp[col + e] : 0;
+            outv[e] = (re == kNonfiniteExp || ce == kNonfiniteExp)
+                          ? nan_value()
+                          : crt_finish(s0[e], s1[e], s2[e], s3[e], f[e], re + ce - K.two_bits, K);
+        }
+        double *dst = P.C + row * P.ldc + col;
+        if (nc == 4 && vec_out && P.out_mode == 0) {
+            reinterpret_cast<double2 *>(dst)[0] = make_double2(outv[0], outv[1]);
+            reinterpret_cast<double2 *>(dst)[1] = make_double2(outv[2], outv[3]);
+        } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                if (e < nc) write_mode(dst + e, outv[e], P.out_mode);
+        }
+    }
+}
+
+template <bool kFused>
+__global__ void __launch_bounds__(gemm_threads(kFused), 1)
     residue_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ GemmParams P) {
@@ -74,7 +182,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint64_t *tfull = empty + kStages;   // [2] accumulator ready
     uint64_t *tempty = tfull + 2;        // [2] accumulator drained by the epilogue
     uint64_t *drain = tempty + 2;        // MMA drain on abort
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    uint64_t *sfull = drain + 1;         // [2] scratch slot complete (fused)
+    uint64_t *sempty = sfull + 2;        // [2] scratch slot consumed by the CRT warps (fused)
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sempty + 2);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -86,7 +196,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], 128);
+            mbar_init(&tempty[a], kEpiThreads);
+            mbar_init(&sfull[a], kEpiThreads);
+            mbar_init(&sempty[a], kCrtThreads);
         }
         mbar_init(drain, 1);
         *abort = 0;
@@ -110,14 +222,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             uint32_t phase = 0;
             uint32_t issued_mask = 0, issued_phase = 0;
             bool ok = true;
-            for (int64_t t = blockIdx.x; t < P.total_tiles && ok; t += gridDim.x) {
-                int mod, tm, tn;
-                decode_tile(P, t, mod, tm, tn);
+            for_each_unit<kFused>(P, [&](int mod, int tm, int tn, int64_t) {
                 for (int kb = 0; kb < P.num_kb; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1, abort)) {
                         raise_error(P, abort, kErrTimeoutProducer);
                         ok = false;
-                        break;
+                        return false;
                     }
                     mbar_arrive_expect_tx(&full[stage], kStageBytes);
                     tma_load_3d(sA + stage * kABytes, &tmA, &full[stage], kb * kBK, tm * kBM, mod);
@@ -129,7 +239,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         phase ^= 1;
                     }
                 }
-            }
+                return true;
+            });
             if (!ok) {
                 // Drain: every issued copy must land before the CTA may exit.
                 for (int s = 0; s < kStages; ++s) {
@@ -151,14 +262,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true, any_issued = false;
-            int64_t local = 0;
-            for (int64_t t = blockIdx.x; t < P.total_tiles && ok; t += gridDim.x, ++local) {
-                const int acc = static_cast<int>(local & 1);
-                const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+            int64_t unit = 0;
+            for_each_unit<kFused>(P, [&](int, int, int, int64_t) {
+                const int acc = static_cast<int>(unit & 1);
+                const uint32_t acc_phase = static_cast<uint32_t>((unit >> 1) & 1);
+                ++unit;
                 if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort)) {
                     raise_error(P, abort, kErrTimeoutMma);
                     ok = false;
-                    break;
+                    return false;
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
@@ -166,7 +278,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     if (!mbar_wait(&full[stage], phase, abort)) {
                         raise_error(P, abort, kErrTimeoutMma);
                         ok = false;
-                        break;
+                        return false;
                     }
                     tc_fence_after();
                     const uint64_t adesc = make_sw128_kmajor_desc(smem_u32(sA + stage * kABytes));
@@ -184,8 +296,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         phase ^= 1;
                     }
                 }
-                if (ok) umma_commit(&tfull[acc]);
-            }
+                umma_commit(&tfull[acc]);
+                return true;
+            });
             if (!ok && any_issued) {
                 umma_commit(drain);
                 const uint32_t a = smem_u32(drain);
@@ -198,32 +311,62 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 }
             }
         }
-    } else {
+    } else if (warp < 6) {
         // ---------------- epilogue (warps 2..5) ----------------
         const int q = warp & 3;  // TMEM lane quadrant this warp may access
         const int row_in_tile = q * 32 + lane;
-        int64_t local = 0;
-        for (int64_t t = blockIdx.x; t < P.total_tiles; t += gridDim.x, ++local) {
-            int mod, tm, tn;
-            decode_tile(P, t, mod, tm, tn);
-            const int acc = static_cast<int>(local & 1);
-            const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+        int64_t unit = 0;
+        for_each_unit<kFused>(P, [&](int mod, int tm, int tn, int64_t tile_local) {
+            const int acc = static_cast<int>(unit & 1);
+            const uint32_t acc_phase = static_cast<uint32_t>((unit >> 1) & 1);
+            ++unit;
+            const int slot_idx = static_cast<int>(tile_local & 1);
+            const uint32_t slot_phase = static_cast<uint32_t>((tile_local >> 1) & 1);
+            if (kFused && mod == 0) {  // the slot must have been consumed by the CRT warps
+                if (!mbar_wait(&sempty[slot_idx], slot_phase ^ 1, abort)) {
+                    raise_error(P, abort, kErrTimeoutEpilogue);
+                    return false;
+                }
+            }
             if (!mbar_wait(&tfull[acc], acc_phase, abort)) {
                 raise_error(P, abort, kErrTimeoutEpilogue);
-                break;
+                return false;
             }
             tc_fence_after();
             const int64_t row = int64_t(tm) * kBM + row_in_tile;
             const uint32_t p = P.mm.p[mod], magic = P.mm.magic[mod], shift = P.mm.shift[mod];
+            const uint32_t off = P.mm.off[mod];
+            const uint32_t u = kFused ? P.crt.u[mod] : 0u;
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(acc * kBN);
+            uint8_t *slot_row =
+                kFused ? P.scratch + (int64_t(blockIdx.x) * 2 + slot_idx) * P.n_mod * kSlotPlaneBytes +
+                             int64_t(mod) * kSlotPlaneBytes + int64_t(row_in_tile) * kBN
+                       : nullptr;
 #pragma unroll 1
             for (int c = 0; c < kBN / 32; ++c) {
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(tbase + c * 32, v);
                 tmem_wait_ld();
                 const int64_t col0 = int64_t(tn) * kBN + c * 32;
-                if (row < P.m && col0 < P.ldo) {
+                if (kFused) {
+                    // t = (r * u) mod p with r = acc mod p; the whole tile row is stored (rows
+                    // and columns past the matrix are skipped by the CRT warps)
+                    uint32_t pk[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        uint32_t w = 0;
+#pragma unroll
+                        for (int b = 0; b < 4; ++b) {
+                            const uint32_t r = mod_acc(v[4 * j + b], p, magic, shift, off);
+                            w |= mod_small(r * u, p, magic, shift) << (8 * b);
+                        }
+                        pk[j] = w;
+                    }
+                    uint4 *dst = reinterpret_cast<uint4 *>(slot_row + c * 32);
+                    dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                    dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                } else if (row < P.m && col0 < P.ldo) {
                     if (!P.out_i32) {
                         uint32_t pk[8];
 #pragma unroll
@@ -231,7 +374,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                             uint32_t w = 0;
 #pragma unroll
                             for (int b = 0; b < 4; ++b)
-                                w |= mod_small(v[4 * j + b], p, magic, shift) << (8 * b);
+                                w |= mod_acc(v[4 * j + b], p, magic, shift, off) << (8 * b);
                             pk[j] = w;
                         }
                         uint8_t *dst = static_cast<uint8_t *>(P.out) + mod * P.plane + row * P.ldo + col0;
@@ -253,6 +396,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             tc_fence_before();
             mbar_arrive(&tempty[acc]);
+            if (kFused && mod == P.n_mod - 1) {
+                __threadfence();  // slot bytes visible at L2 before the CRT warps read them
+                mbar_arrive(&sfull[slot_idx]);
+            }
+            return true;
+        });
+    } else if (kFused) {
+        // ---------------- CRT warps (6..9, fused mode) ----------------
+        const int ct = threadIdx.x - 192;
+        const int64_t tiles = int64_t(P.tiles_m) * P.tiles_n;
+        int64_t local = 0;
+        for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
+            int tm, tn;
+            decode_tile(P, t, tm, tn);
+            const int slot_idx = static_cast<int>(local & 1);
+            const uint32_t slot_phase = static_cast<uint32_t>((local >> 1) & 1);
+            if (!mbar_wait(&sfull[slot_idx], slot_phase, abort)) {
+                raise_error(P, abort, kErrTimeoutEpilogue);
+                break;
+            }
+            const uint8_t *slot =
+                P.scratch + (int64_t(blockIdx.x) * 2 + slot_idx) * P.n_mod * kSlotPlaneBytes;
+            crt_tile(P, slot, tm, tn, ct);
+            mbar_arrive(&sempty[slot_idx]);
         }
     }
 
@@ -306,6 +473,37 @@ static bool make_plane_map(CUtensorMap *map, const void *base, int64_t kdim, int
     return r == CUDA_SUCCESS;
 }
 
+template <bool kFused>
+static cudaError_t configure(int dev) {
+    static int configured = -1;  // last device configured
+    if (configured == dev) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(residue_gemm_kernel<kFused>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kGemmSmemBytes));
+    if (e == cudaSuccess) configured = dev;
+    return e;
+}
+
+static cudaError_t fill_common(GemmParams &P, CUtensorMap &tmA, CUtensorMap &tmB,
+                               const int8_t *a_res, const int8_t *b_res, int64_t m, int64_t n,
+                               int64_t kdim, int64_t ld, int n_mod, const ModMagic &mm, int *err) {
+    // kdim == 0 is handled by the callers; a map needs at least one column
+    const int64_t kd = kdim > 0 ? kdim : 1;
+    if (!make_plane_map(&tmA, a_res, kd, m, ld, n_mod, kBM)) return cudaErrorInvalidValue;
+    if (!make_plane_map(&tmB, b_res, kd, n, ld, n_mod, kBN)) return cudaErrorInvalidValue;
+    std::memset(&P, 0, sizeof(P));
+    P.m = m;
+    P.n = n;
+    P.num_kb = static_cast<int>((kdim + kBK - 1) / kBK);
+    P.n_mod = n_mod;
+    P.tiles_m = static_cast<int>((m + kBM - 1) / kBM);
+    P.tiles_n = static_cast<int>((n + kBN - 1) / kBN);
+    P.total_units = int64_t(P.tiles_m) * P.tiles_n * n_mod;
+    P.mm = mm;
+    P.err = err;
+    return P.num_kb > 0 ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 int gemm_smem_bytes() { return static_cast<int>(kGemmSmemBytes); }
 
 // Launch R[i] = (A_i @ B_i^T) mod p_i over n_mod planes.
@@ -317,39 +515,59 @@ cudaError_t launch_residue_gemm(const int8_t *a_res, const int8_t *b_res, int64_
                                 void *out, int64_t ldo, int out_i32, int *err, int num_sms,
                                 cudaStream_t stream) {
     if (m == 0 || n == 0 || n_mod == 0) return cudaSuccess;
-    static int configured_device = -1;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (configured_device != dev) {
-        cudaError_t e = cudaFuncSetAttribute(residue_gemm_kernel,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(kGemmSmemBytes));
-        if (e != cudaSuccess) return e;
-        configured_device = dev;
-    }
+    cudaError_t e = configure<false>(dev);
+    if (e != cudaSuccess) return e;
     CUtensorMap tmA, tmB;
-    // kdim == 0 still needs a valid map: describe one zero column (never loaded).
-    const int64_t kd = kdim > 0 ? kdim : 1;
-    if (!make_plane_map(&tmA, a_res, kd, m, ld, n_mod, kBM)) return cudaErrorInvalidValue;
-    if (!make_plane_map(&tmB, b_res, kd, n, ld, n_mod, kBN)) return cudaErrorInvalidValue;
     GemmParams P;
-    P.m = m;
-    P.n = n;
-    P.num_kb = static_cast<int>((kdim + kBK - 1) / kBK);
-    P.n_mod = n_mod;
-    P.tiles_m = static_cast<int>((m + kBM - 1) / kBM);
-    P.tiles_n = static_cast<int>((n + kBN - 1) / kBN);
-    P.total_tiles = int64_t(P.tiles_m) * P.tiles_n * n_mod;
+    e = fill_common(P, tmA, tmB, a_res, b_res, m, n, kdim, ld, n_mod, mm, err);
+    if (e != cudaSuccess) return e;
     P.out = out;
     P.ldo = ldo;
     P.plane = m * ldo;
     P.out_i32 = out_i32;
-    P.mm = mm;
-    P.err = err;
-    if (P.num_kb == 0) return cudaErrorInvalidValue;  // callers handle k == 0
-    int64_t grid = P.total_tiles < num_sms ? P.total_tiles : num_sms;
-    residue_gemm_kernel<<<static_cast<unsigned>(grid), kGemmThreads, kGemmSmemBytes, stream>>>(
-        tmA, tmB, P);
+    const int64_t grid = P.total_units < num_sms ? P.total_units : num_sms;
+    residue_gemm_kernel<false><<<static_cast<unsigned>(grid), gemm_threads(false), kGemmSmemBytes,
+                                 stream>>>(tmA, tmB, P);
+    return cudaGetLastError();
+}
+
+// Output tiles of 128 x 256 for an m x n product.
+int64_t gemm_output_tiles(int64_t m, int64_t n) {
+    return ((m + kBM - 1) / kBM) * ((n + kBN - 1) / kBN);
+}
+
+// Scratch bytes of the fused kernel: 2 slots of n_mod x 128 x 256 bytes per CTA.
+size_t fused_scratch_bytes(int n_mod, int num_ctas) {
+    return size_t(num_ctas) * 2 * size_t(n_mod) * size_t(kSlotPlaneBytes);
+}
+
+// Fused K2+K3: C (op)= CRT(A_i @ B_i^T mod p_i) with the exponent scaling.  `grid` CTAs,
+// scratch of fused_scratch_bytes(n_mod, grid).
+cudaError_t launch_fused_gemm_crt(const int8_t *a_res, const int8_t *b_res, int64_t m, int64_t n,
+                                  int64_t kdim, int64_t ld, const CrtConst &K,
+                                  const int32_t *row_exp, const int32_t *col_exp, double *C,
+                                  int64_t ldc, int out_mode, uint8_t *scratch, int grid, int *err,
+                                  cudaStream_t stream) {
+    if (m == 0 || n == 0) return cudaSuccess;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaError_t e = configure<true>(dev);
+    if (e != cudaSuccess) return e;
+    CUtensorMap tmA, tmB;
+    GemmParams P;
+    e = fill_common(P, tmA, tmB, a_res, b_res, m, n, kdim, ld, K.n_mod, K.mm, err);
+    if (e != cudaSuccess) return e;
+    P.scratch = scratch;
+    P.row_exp = row_exp;
+    P.col_exp = col_exp;
+    P.C = C;
+    P.ldc = ldc;
+    P.out_mode = out_mode;
+    P.crt = K;
+    residue_gemm_kernel<true><<<static_cast<unsigned>(grid), gemm_threads(true), kGemmSmemBytes,
+                                stream>>>(tmA, tmB, P);
     return cudaGetLastError();
 }
 

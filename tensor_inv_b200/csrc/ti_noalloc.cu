@@ -20,7 +20,7 @@
 // the caller.
 #include <atomic>
 
-#include "../../include/tensor_inv_crt.h"
+#include "tensor_inv_crt.h"
 
 namespace {
 

@@ -5,7 +5,9 @@
 // with element (o, l) at X[o*s_outer + l*s_k].  Two passes:
 //   1. exponent: e_o = frexp(max(max_l |x_ol|, 1e-300)).exponent (or kNonfiniteExp)
 //   2. split:    v = round_half_even(x * 2^(bits - e_o)) computed from the float64 bits,
-//                r_i = v mod p_i in [0, p_i), written K-major as res[i][o][l] (int8).
+//                r_i = v mod p_i in [0, p_i) (the reference's floor mod; or, for the
+//                opt-in wide moduli up to 255, the symmetric residue in
+//                [-(p_i-1)/2, (p_i-1)/2]), written K-major as res[i][o][l] (int8).
 // Two layouts of the source are handled without copies: k contiguous (s_k == 1, "rows")
 // and outer contiguous (s_outer == 1, "cols", a transposed view), the latter through a
 // shared-memory transpose.  Both write 8 consecutive residues per thread and modulus
@@ -51,7 +53,8 @@ __device__ __forceinline__ uint64_t scaled_magnitude(double x, int bits, int e, 
 }
 
 // Residue bytes of 8 signed values (magnitudes mag[j] < 2^53, signs neg[j]) mod p_i,
-// packed little-endian into two 32-bit words.
+// packed little-endian into two 32-bit words.  kSym selects symmetric residues.
+template <bool kSym>
 __device__ __forceinline__ uint2 residues8(const uint32_t (&a2)[8], const uint32_t (&a1)[8],
                                            const uint32_t (&a0)[8], uint32_t negmask,
                                            const SplitConst &C, int i) {
@@ -62,8 +65,16 @@ __device__ __forceinline__ uint2 residues8(const uint32_t (&a2)[8], const uint32
     for (int j = 0; j < 8; ++j) {
         // mag = a2*2^32 + a1*2^16 + a0  ==>  t == mag (mod p), t < 2^29
         uint32_t t = a2[j] * w32 + a1[j] * w16 + a0[j];
-        t = ((negmask >> j) & 1u) ? bigp - t : t;  // -mag (mod p), still < 2^30
-        const uint32_t r = mod_small(t, p, magic, shift);
+        uint32_t r;
+        if (!kSym) {
+            t = ((negmask >> j) & 1u) ? bigp - t : t;  // -mag (mod p), still < 2^30
+            r = mod_small(t, p, magic, shift);
+        } else {
+            int32_t rs = static_cast<int32_t>(mod_small(t, p, magic, shift));
+            rs = rs > static_cast<int32_t>(p >> 1) ? rs - static_cast<int32_t>(p) : rs;
+            rs = ((negmask >> j) & 1u) ? -rs : rs;
+            r = static_cast<uint32_t>(rs) & 0xFFu;
+        }
         out[j >> 2] |= r << (8 * (j & 3));
     }
     return make_uint2(out[0], out[1]);
@@ -143,6 +154,7 @@ __global__ void exp_cols_kernel(const double *__restrict__ X, int64_t outer, int
 // ---------------------------------------------------------------------------------------
 
 // k contiguous.  Each thread owns 8 consecutive elements of one vector.
+template <bool kSym>
 __global__ void __launch_bounds__(256) split_rows_kernel(
     const double *__restrict__ X, int64_t outer, int64_t kdim, int64_t s_outer,
     const int32_t *__restrict__ exps, int8_t *__restrict__ res, int64_t ld_res,
@@ -172,7 +184,7 @@ __global__ void __launch_bounds__(256) split_rows_kernel(
         decompose8(v, C.bits, e, a2, a1, a0, negmask);
         int8_t *dst = res + o * ld_res + l0;
         for (int i = 0; i < C.n_mod; ++i) {
-            const uint2 w = residues8(a2, a1, a0, negmask, C, i);
+            const uint2 w = residues8<kSym>(a2, a1, a0, negmask, C, i);
             *reinterpret_cast<uint2 *>(dst + i * plane) = w;
         }
     }
@@ -183,6 +195,7 @@ __global__ void __launch_bounds__(256) split_rows_kernel(
 // consecutive k of one vector.
 constexpr int kColTileK = 64, kColTileO = 32, kColPad = 66;  // row pitch in doubles
 
+template <bool kSym>
 __global__ void __launch_bounds__(256) split_cols_kernel(
     const double *__restrict__ X, int64_t outer, int64_t kdim, int64_t s_k,
     const int32_t *__restrict__ exps, int8_t *__restrict__ res, int64_t ld_res,
@@ -222,7 +235,7 @@ __global__ void __launch_bounds__(256) split_cols_kernel(
             decompose8(v, C.bits, e, a2, a1, a0, negmask);
             int8_t *dst = res + o * ld_res + lc;
             for (int i = 0; i < C.n_mod; ++i) {
-                const uint2 w = residues8(a2, a1, a0, negmask, C, i);
+                const uint2 w = residues8<kSym>(a2, a1, a0, negmask, C, i);
                 *reinterpret_cast<uint2 *>(dst + i * plane) = w;
             }
         }
@@ -247,8 +260,12 @@ cudaError_t launch_split(const double *X, int64_t outer, int64_t kdim, int64_t s
         const int64_t total = outer * (ld_res >> 3);
         int64_t sblocks = (total + 255) / 256;
         if (sblocks > int64_t(num_sms) * 8) sblocks = int64_t(num_sms) * 8;
-        split_rows_kernel<<<static_cast<unsigned>(sblocks), 256, 0, stream>>>(
-            X, outer, kdim, s_outer, exp_out, res, ld_res, plane, C);
+        if (C.symmetric)
+            split_rows_kernel<true><<<static_cast<unsigned>(sblocks), 256, 0, stream>>>(
+                X, outer, kdim, s_outer, exp_out, res, ld_res, plane, C);
+        else
+            split_rows_kernel<false><<<static_cast<unsigned>(sblocks), 256, 0, stream>>>(
+                X, outer, kdim, s_outer, exp_out, res, ld_res, plane, C);
     } else {
         const int64_t blocks = (outer + 31) / 32;
         exp_cols_kernel<<<static_cast<unsigned>(blocks), 1024, 0, stream>>>(X, outer, kdim, s_k,
@@ -257,8 +274,12 @@ cudaError_t launch_split(const double *X, int64_t outer, int64_t kdim, int64_t s
                               ((ld_res + kColTileK - 1) / kColTileK);
         int64_t sblocks = tiles;
         if (sblocks > int64_t(num_sms) * 8) sblocks = int64_t(num_sms) * 8;
-        split_cols_kernel<<<static_cast<unsigned>(sblocks), 256, 0, stream>>>(
-            X, outer, kdim, s_k, exp_out, res, ld_res, plane, C);
+        if (C.symmetric)
+            split_cols_kernel<true><<<static_cast<unsigned>(sblocks), 256, 0, stream>>>(
+                X, outer, kdim, s_k, exp_out, res, ld_res, plane, C);
+        else
+            split_cols_kernel<false><<<static_cast<unsigned>(sblocks), 256, 0, stream>>>(
+                X, outer, kdim, s_k, exp_out, res, ld_res, plane, C);
     }
     return cudaGetLastError();
 }

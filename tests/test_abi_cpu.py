@@ -65,6 +65,12 @@ def test_workspace_sizes(nat):
     # 8192^3 at float64: 25 moduli x (A + B + product) int8 planes + exponents
     ws = nat.crt_workspace_size(8192, 8192, 8192, 53)
     assert 25 * 3 * 8192 * 8192 <= ws <= 25 * 3 * 8192 * 8192 + 4 * 2 * 8192 + 4096
+    # the wide moduli need 16 planes instead of 25 at the same precision
+    ws16 = nat.crt_workspace_size_ex(8192, 8192, 8192, 53, nat.options("wide"))
+    assert 16 * 3 * 8192 * 8192 <= ws16 <= 16 * 3 * 8192 * 8192 + 4 * 2 * 8192 + 4096
+    # 1024^3: A, B and product planes
+    ws = nat.crt_workspace_size(1024, 1024, 1024, 53)
+    assert 24 * 3 * 1024 * 1024 <= ws <= 24 * 3 * 1024 * 1024 + 4 * 2 * 1024 + 4096
     assert nat.crt_workspace_size(37, 29, 51, 53) > 0
     with pytest.raises(nat.NativeError):
         nat.crt_workspace_size(10, 10, nat.TI_MAX_K + 1, 53)
@@ -97,3 +103,21 @@ def test_product_does_not_import_oracle():
     for src in list(pkg.rglob("*.py")) + list(pkg.rglob("*.cu")) + list(pkg.rglob("*.cuh")):
         text = src.read_text()
         assert "oracle" not in re.sub(r"(#|//).*", "", text), src
+
+
+def test_moduli_plans(nat):
+    """Wide moduli: the fewest that keep 53 bits; a fixed count lowers the precision."""
+    assert nat.crt_plan(8192, 53) == (25, 53, [3, 5, 7, 11, 13, 17, 19, 23, 29, 31, 37, 41,
+                                                43, 47, 53, 59, 61, 67, 71, 73, 79, 83, 89, 97, 101])
+    n, b, mods = nat.crt_plan(8192, 53, "wide")
+    assert (n, b) == (16, 53) and mods[:4] == [255, 253, 251, 247]
+    assert [nat.crt_plan(8192, 53, "wide", N)[1] for N in (12, 13, 14, 15, 16)] == [40, 44, 47,
+                                                                                      51, 53]
+    assert nat.crt_plan(1024, 53, "wide")[:2] == (15, 53)
+    import math
+    for N in range(1, 17):  # the wide moduli are pairwise coprime and below 2^127 together
+        mods = nat.crt_plan(8, 53, "wide", N)[2]
+        assert all(math.gcd(a, c) == 1 for i, a in enumerate(mods) for c in mods[i + 1:])
+        assert math.prod(mods) < 2**127
+    with pytest.raises(ValueError):
+        nat.crt_plan(8192, 53, "wide", 17)

@@ -244,3 +244,140 @@ def test_empty_outputs(ti):
     B = torch.randn(5, 3, dtype=torch.float64, device="cuda")
     assert ti.crt_matmul(A, B).shape == (0, 3)
     assert ti.crt_matmul(B.T, B[:, :0]).shape == (3, 0)
+
+
+# ---------------------------------------------------------------------------------------
+# fused GEMM+CRT kernel (opt-in with TI_CRT_PATH=fused)
+# ---------------------------------------------------------------------------------------
+@pytest.fixture
+def crt_path(monkeypatch):
+    def set_path(p):
+        monkeypatch.setenv("TI_CRT_PATH", p)
+    return set_path
+
+
+@pytest.mark.parametrize("m,n,k,phi", [(300, 500, 257, 2.0), (129, 257, 1, None),
+                                       (133, 77, 1100, 1.0), (128, 256, 128, None),
+                                       (200, 600, 7200, 0.5)])
+def test_fused_path_vs_oracle(ti, oracle, crt_path, m, n, k, phi):
+    crt_path("fused")
+    A = _rand((m, k), 3000 + m, phi)
+    B = _rand((k, n), 4000 + n, phi)
+    want = oracle.crt_matmul(A.numpy(), B.numpy(), 53)
+    _assert_bitexact(ti.crt_matmul(A.cuda(), B.cuda()), want)
+
+
+def test_fused_equals_unfused_large(ti, oracle, crt_path):
+    m, n, k = 2304, 4100, 513      # 18 x 17 = 306 output tiles
+    A = _rand((m, k), 71, 1.5).cuda()
+    B = _rand((k, n), 72, 1.5).cuda()
+    crt_path("fused")
+    C_auto = ti.crt_matmul(A, B)
+    crt_path("unfused")
+    C_unf = ti.crt_matmul(A, B)
+    _assert_bitexact(C_auto, C_unf.cpu().numpy())
+    for (r0, r1, c0, c1) in [(0, 64, 0, 64), (2250, 2304, 4050, 4100)]:
+        want = oracle.crt_matmul(A[r0:r1].cpu().numpy(), B[:, c0:c1].cpu().numpy(), 53)
+        _assert_bitexact(C_auto[r0:r1, c0:c1], want)
+
+
+@pytest.mark.parametrize("alpha", [-1, 1])
+def test_fused_update_modes(ti, oracle, crt_path, alpha):
+    crt_path("fused")
+    m, n, k = 300, 270, 256
+    A = _rand((m, k), 81)
+    B = _rand((k, n), 82)
+    C0 = _rand((m, n), 83)
+    prod = oracle.crt_matmul(A.numpy(), B.numpy(), 53)
+    want = C0.numpy() - prod if alpha == -1 else C0.numpy() + prod
+    C = C0.cuda()
+    ti.crt_matmul_update(C, A.cuda(), B.cuda(), alpha=alpha)
+    _assert_bitexact(C, want)
+
+
+def test_fused_nonfinite(ti, oracle, crt_path):
+    crt_path("fused")
+    A = _rand((40, 60), 91)
+    B = _rand((60, 30), 92)
+    A[3, 7] = float("nan")
+    B[5, 11] = float("inf")
+    C = ti.crt_matmul(A.cuda(), B.cuda()).cpu()
+    assert torch.isnan(C[3]).all() and torch.isnan(C[:, 11]).all()
+    keep_r = [i for i in range(40) if i != 3]
+    keep_c = [j for j in range(30) if j != 11]
+    want = oracle.crt_matmul(A[keep_r].numpy(), B[:, keep_c].numpy(), 53)
+    _assert_bitexact(C[keep_r][:, keep_c], want)
+
+
+# ---------------------------------------------------------------------------------------
+# opt-in wide moduli (pairwise-coprime odd moduli <= 255, the survey's config 2)
+# ---------------------------------------------------------------------------------------
+@pytest.mark.parametrize("case", golden_cases())
+def test_wide_moduli_full_precision_is_bit_identical(ti, case):
+    """Automatic wide count keeps every bit: the reference's own outputs, bit for bit."""
+    g = _golden(case)
+    dt = DTYPES[str(g["dtype"])]
+    A = torch.from_numpy(g["A"]).to(dt).cuda()
+    B = torch.from_numpy(g["B"]).to(dt).cuda()
+    _assert_bitexact(ti.crt_matmul(A, B, moduli="wide"), g["out"])
+
+
+@pytest.mark.parametrize("m,n,k,phi", [(300, 500, 257, 2.0), (133, 77, 1100, 1.0),
+                                       (200, 600, 7200, 0.5), (1024, 1024, 1024, None)])
+def test_wide_moduli_vs_reference_scheme(ti, oracle, m, n, k, phi):
+    A = _rand((m, k), 5000 + m, phi)
+    B = _rand((k, n), 6000 + n, phi)
+    want = oracle.crt_matmul(A.numpy(), B.numpy(), 53)
+    _assert_bitexact(ti.crt_matmul(A.cuda(), B.cuda(), moduli="wide"), want)
+
+
+@pytest.mark.parametrize("n_mod", [12, 13, 14, 15, 16])
+@pytest.mark.parametrize("moduli", ["wide", "primes"])
+def test_moduli_sweep_vs_oracle(ti, oracle, n_mod, moduli):
+    """Config-2 sweep: N moduli, precision lowered to what N moduli can hold; bit-exact
+    against the reference algorithm restated with the same moduli and precision."""
+    from tensor_inv_b200 import _native
+
+    m, n, k = 96, 80, 8192
+    A = _rand((m, k), 7000 + n_mod, 2.0)
+    B = _rand((k, n), 8000 + n_mod, 2.0)
+    N, bits, mods = _native.crt_plan(k, 53, moduli, n_mod)
+    assert N == n_mod and bits <= 53
+    want = oracle.crt_matmul_moduli(A.numpy(), B.numpy(), mods, bits)
+    got = ti.crt_matmul(A.cuda(), B.cuda(), moduli=moduli, n_moduli=n_mod)
+    _assert_bitexact(got, want)
+
+
+def test_wide_moduli_transposed_and_update(ti, oracle, crt_path):
+    m, n, k = 190, 150, 333
+    A = _rand((k, m), 17, 1.0).T
+    B = _rand((n, k), 18, 1.0).T
+    want = oracle.crt_matmul(A.numpy(), B.numpy(), 53)
+    _assert_bitexact(ti.crt_matmul(A.cuda(), B.cuda(), moduli="wide"), want)
+    crt_path("fused")
+    _assert_bitexact(ti.crt_matmul(A.cuda(), B.cuda(), moduli="wide"), want)
+    C0 = _rand((m, n), 19)
+    C = C0.cuda()
+    ti.crt_matmul_update(C, A.cuda(), B.cuda(), alpha=-1, moduli="wide")
+    _assert_bitexact(C, C0.numpy() - want)
+
+
+def test_wide_moduli_large_blocks(ti, oracle):
+    m = n = k = 4096
+    A = _rand((m, k), 63, 2.0)
+    B = _rand((k, n), 64, 2.0)
+    C = ti.crt_matmul(A.cuda(), B.cuda(), moduli="wide").cpu()
+    for (r0, r1, c0, c1) in [(0, 64, 0, 48), (4030, 4096, 4040, 4096)]:
+        want = oracle.crt_matmul(A[r0:r1].numpy(), B[:, c0:c1].numpy(), 53)
+        _assert_bitexact(C[r0:r1, c0:c1], want)
+
+
+def test_moduli_errors(ti):
+    A = torch.randn(4, 5, dtype=torch.float64, device="cuda")
+    with pytest.raises(ValueError):
+        ti.crt_matmul(A, A.T, moduli="octal")
+    with pytest.raises(ValueError):
+        ti.crt_matmul(A, A.T, moduli="wide", n_moduli=17)
+    with pytest.raises(ValueError):
+        big = torch.zeros(1, 133145, dtype=torch.float64, device="cuda")
+        ti.crt_matmul(big, big.T, moduli="wide")
