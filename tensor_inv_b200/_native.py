@@ -30,6 +30,7 @@ TI_MODULI_WIDE = 1
 
 TI_NONFINITE_EXP = -(2**31)
 TI_MAX_K = 135263
+TI_MAX_K_WIDE = 133144
 
 # name -> (restype, argtypes); mirrors include/tensor_inv_crt.h
 _i64, _int, _p, _sz = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t
@@ -150,6 +151,10 @@ def crt_plan(k: int, bits: int, moduli=None, n_moduli=None):
     st = lib().ti_crt_plan(int(k), int(bits), ctypes.byref(o), ctypes.byref(n), ctypes.byref(b),
                            mods)
     if st == TI_ERR_UNSUPPORTED:
+        limit = TI_MAX_K if moduli in (None, "primes") else TI_MAX_K_WIDE
+        if k > limit:
+            raise ValueError(f"inner dim {k} exceeds {limit}, the bound that keeps the int32 "
+                             f"residue accumulators exact for moduli {moduli or 'primes'!r}")
         raise ValueError(f"no moduli plan for inner dim {k}, bits {bits}, moduli {moduli!r}, "
                          f"n_moduli {n_moduli!r}")
     check("ti_crt_plan", st)

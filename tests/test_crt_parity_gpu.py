@@ -234,7 +234,7 @@ def test_errors(ti):
     with pytest.raises(ValueError):
         from tensor_inv_b200.crt_matmul import _n_moduli
         _n_moduli(2**62, 53)
-    with pytest.raises(RuntimeError):
+    with pytest.raises(ValueError, match="accumulator"):
         big = torch.zeros(1, 135264, dtype=torch.float64, device="cuda")
         ti.crt_matmul(big, big.T)
 
