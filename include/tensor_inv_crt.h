@@ -123,8 +123,14 @@ typedef struct ti_crt_options {
                                (PRIMES <= 25, WIDE <= 16); when they cannot hold 2*k*2^(2*bits)
                                the precision is lowered to the largest b with
                                prod(moduli) > 2*k*2^(2*b), the config-2 moduli sweep */
-    void *stage_events[4];  /* optional cudaEvent_t, recorded on the stream before K1, before
-                               K2, before K3 and after K3; NULL entries are skipped */
+    void *stage_events[4];  /* optional cudaEvent_t, recorded before K1, before the first K2,
+                               after the last K2 (before the last K3) and at the end; NULL
+                               entries are skipped */
+    int bands;              /* 0 or 1: one band, all stages in order on `stream`.  n > 1 splits
+                               A into n row bands pipelined over two internal streams: the GEMM
+                               of band b overlaps the split of band b+1 and the reconstruction
+                               of band b-1 (opt-in: on B200 the shared SMs slow the GEMM more
+                               than the overlap saves) */
 } ti_crt_options_t;
 
 /* The moduli count, the precision actually kept, and (if moduli_out != NULL, room for 32)

@@ -40,7 +40,7 @@ class CrtOptions(ctypes.Structure):
     """ti_crt_options_t."""
 
     _fields_ = [("moduli", ctypes.c_int), ("n_moduli", ctypes.c_int),
-                ("stage_events", ctypes.c_void_p * 4)]
+                ("stage_events", ctypes.c_void_p * 4), ("bands", ctypes.c_int)]
 
 
 _opt = ctypes.POINTER(CrtOptions)
@@ -124,8 +124,8 @@ def crt_workspace_size(m: int, n: int, k: int, bits: int) -> int:
     return out.value
 
 
-def options(moduli=None, n_moduli=None, events=None) -> CrtOptions:
-    """ti_crt_options_t from Python values: moduli None/'primes' or 'wide'."""
+def options(moduli=None, n_moduli=None, events=None, bands=0) -> CrtOptions:
+    """ti_crt_options_t from Python values: moduli None/'primes' or 'wide'; bands 0 = auto."""
     if moduli in (None, "primes"):
         kind = TI_MODULI_PRIMES
     elif moduli == "wide":
@@ -136,6 +136,7 @@ def options(moduli=None, n_moduli=None, events=None) -> CrtOptions:
     if n < 0:
         raise ValueError("n_moduli must be positive")
     o = CrtOptions(kind, n)
+    o.bands = int(bands)
     if events is not None:
         for i, e in enumerate(events):
             o.stage_events[i] = e

@@ -5,6 +5,7 @@
 // stage sequence K1 (split) -> K2 (tcgen05 residue GEMM) -> K3 (exact CRT).
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 
 #include "tensor_inv_crt.h"
 #include "ti_common.cuh"
@@ -12,15 +13,17 @@
 namespace ti {
 cudaError_t launch_split(const double *X, int64_t outer, int64_t kdim, int64_t s_outer,
                          int64_t s_k, const SplitConst &C, int32_t *exp_out, int8_t *res,
-                         int64_t ld_res, int num_sms, cudaStream_t stream);
+                         int64_t ld_res, int num_sms, cudaStream_t stream, int64_t plane = 0,
+                         int blocks_per_sm = 8);
 cudaError_t launch_residue_gemm(const int8_t *a_res, const int8_t *b_res, int64_t m, int64_t n,
                                 int64_t kdim, int64_t ld, int n_mod, const ModMagic &mm,
                                 void *out, int64_t ldo, int out_i32, int *err, int num_sms,
-                                cudaStream_t stream);
+                                cudaStream_t stream, int64_t a_plane = 0, int64_t b_plane = 0,
+                                int64_t out_plane = 0);
 cudaError_t launch_crt(const void *R, bool in_u8, int64_t ldr, int64_t plane, int64_t rows,
                        int64_t cols, const int32_t *row_exp, const int32_t *col_exp, double *C,
                        int64_t ldc, int out_mode, const CrtConst &K, int num_sms,
-                       cudaStream_t stream);
+                       cudaStream_t stream, int blocks_per_sm = 8);
 int64_t gemm_output_tiles(int64_t m, int64_t n);
 size_t fused_scratch_bytes(int n_mod, int num_ctas);
 cudaError_t launch_fused_gemm_crt(const int8_t *a_res, const int8_t *b_res, int64_t m, int64_t n,
@@ -254,6 +257,50 @@ static int device_info(DevInfo &d) {
 static int cuda_status(cudaError_t e) { return e == cudaSuccess ? TI_OK : TI_ERR_CUDA; }
 
 // ---------------------------------------------------------------------------------------
+// per-device streams and events of the banded pipeline (created once, kept until exit)
+// ---------------------------------------------------------------------------------------
+constexpr int kMaxBands = 8;
+constexpr int kMaxDevices = 64;
+constexpr int kSideBlocksPerSm = 2;  // split/CRT blocks per SM while a GEMM is resident
+
+struct Pipeline {
+    std::mutex mu;                   // held while a call records and waits on the events
+    bool ready = false;
+    cudaStream_t hi = nullptr;       // GEMMs (highest priority)
+    cudaStream_t lo = nullptr;       // splits and reconstructions (lowest priority)
+    cudaEvent_t fork = nullptr, hi_done = nullptr, lo_done = nullptr;
+    cudaEvent_t split_done[kMaxBands] = {}, gemm_done[kMaxBands] = {};
+};
+
+static Pipeline g_pipe[kMaxDevices];
+
+static int pipeline_for_device(int dev, Pipeline *&out) {
+    if (dev < 0 || dev >= kMaxDevices) return TI_ERR_UNSUPPORTED;
+    Pipeline &P = g_pipe[dev];
+    out = &P;
+    if (P.ready) return TI_OK;
+    int least = 0, greatest = 0;
+    if (cudaDeviceGetStreamPriorityRange(&least, &greatest) != cudaSuccess) return TI_ERR_CUDA;
+    if (cudaStreamCreateWithPriority(&P.hi, cudaStreamNonBlocking, greatest) != cudaSuccess ||
+        cudaStreamCreateWithPriority(&P.lo, cudaStreamNonBlocking, least) != cudaSuccess)
+        return TI_ERR_CUDA;
+    cudaEvent_t *evs[] = {&P.fork, &P.hi_done, &P.lo_done};
+    for (cudaEvent_t *e : evs)
+        if (cudaEventCreateWithFlags(e, cudaEventDisableTiming) != cudaSuccess) return TI_ERR_CUDA;
+    for (int b = 0; b < kMaxBands; ++b)
+        if (cudaEventCreateWithFlags(&P.split_done[b], cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&P.gemm_done[b], cudaEventDisableTiming) != cudaSuccess)
+            return TI_ERR_CUDA;
+    P.ready = true;
+    return TI_OK;
+}
+
+// Automatic banding of device-resident operands: one band.  Measured on B200 at 8192^3,
+// splits and reconstructions sharing SMs with the GEMM slow it by more (5.6 -> 8.7 ms) than
+// the integer work they hide (3.5 ms), so overlap is opt-in (options.bands > 1).
+static int auto_bands(int64_t) { return 1; }
+
+// ---------------------------------------------------------------------------------------
 // int8 repacking for the reference-layout batched GEMM entry point
 // ---------------------------------------------------------------------------------------
 // dst[b][r][0..ld) = src[b][r][0..K) followed by zeros
@@ -474,6 +521,84 @@ static void record(void *const *ev, int i, cudaStream_t s) {
     if (ev && ev[i]) cudaEventRecord(static_cast<cudaEvent_t>(ev[i]), s);
 }
 
+// The banded pipeline: A split into row bands of band_rows (a multiple of 128).
+//   hi: K1(B), K1(A_0) | GEMM(0) | GEMM(1) | ... each GEMM(b) after split_done[b]
+//   lo: K1(A_{b+1}) -> split_done[b+1]; wait gemm_done[b]; K3(b)     for b = 0 .. bands-1
+// so the GEMM of band b (tensor cores) overlaps the integer work of the split of band b+1
+// and the reconstruction of band b-1.  Both streams fork from and join back to `s`.
+static int crt_matmul_banded(const double *A, int64_t sa0, int64_t sa1, const double *B,
+                             int64_t sb0, int64_t sb1, double *C, int64_t ldc, int64_t m,
+                             int64_t n, int64_t k, int out_mode, void *const *ev,
+                             cudaStream_t s, const CrtLayout &L, const SplitConst &SC,
+                             const CrtConst &KC, const DevInfo &d, int bands, int64_t band_rows,
+                             int32_t *rexp, int32_t *cexp, int8_t *ares, int8_t *bres,
+                             uint8_t *R) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return TI_ERR_CUDA;
+    Pipeline *PP = nullptr;
+    std::lock_guard<std::mutex> lock(g_pipe[dev < 0 || dev >= kMaxDevices ? 0 : dev].mu);
+    int rc = pipeline_for_device(dev, PP);
+    if (rc != TI_OK) return rc;
+    Pipeline &P = *PP;
+    const int64_t a_plane = m * L.ldk, b_plane = n * L.ldk, r_plane = m * L.ldr;
+    auto split_a = [&](int b, cudaStream_t st, int bps) {
+        const int64_t r0 = int64_t(b) * band_rows;
+        const int64_t rows = m - r0 < band_rows ? m - r0 : band_rows;
+        const double *Ab = A + r0 * sa0;
+        if (sa1 == 1)
+            return launch_split(Ab, rows, k, sa0, 1, SC, rexp + r0, ares + r0 * L.ldk, L.ldk,
+                                d.num_sms, st, a_plane, bps);
+        return launch_split(Ab, rows, k, 1, sa1, SC, rexp + r0, ares + r0 * L.ldk, L.ldk,
+                            d.num_sms, st, a_plane, bps);
+    };
+    record(ev, 0, s);
+    if (cudaEventRecord(P.fork, s) != cudaSuccess) return TI_ERR_CUDA;
+    if (cudaStreamWaitEvent(P.hi, P.fork, 0) != cudaSuccess ||
+        cudaStreamWaitEvent(P.lo, P.fork, 0) != cudaSuccess)
+        return TI_ERR_CUDA;
+    // hi: B and the first band of A, at full occupancy (nothing to overlap yet)
+    cudaError_t e;
+    if (sb0 == 1) e = launch_split(B, n, k, sb1, 1, SC, cexp, bres, L.ldk, d.num_sms, P.hi);
+    else e = launch_split(B, n, k, 1, sb0, SC, cexp, bres, L.ldk, d.num_sms, P.hi);
+    if (e != cudaSuccess) return TI_ERR_CUDA;
+    if (split_a(0, P.hi, 8) != cudaSuccess) return TI_ERR_CUDA;
+    if (cudaEventRecord(P.split_done[0], P.hi) != cudaSuccess) return TI_ERR_CUDA;
+    // lo waits for B's residues before any band split (the split of A needs nothing from B,
+    // but sharing SMs with K1(B) would only delay the first GEMM)
+    if (cudaStreamWaitEvent(P.lo, P.split_done[0], 0) != cudaSuccess) return TI_ERR_CUDA;
+    record(ev, 1, P.hi);
+    for (int b = 0; b < bands; ++b) {
+        const int64_t r0 = int64_t(b) * band_rows;
+        const int64_t rows = m - r0 < band_rows ? m - r0 : band_rows;
+        // hi: GEMM(b)
+        if (b > 0 && cudaStreamWaitEvent(P.hi, P.split_done[b], 0) != cudaSuccess)
+            return TI_ERR_CUDA;
+        e = launch_residue_gemm(ares + r0 * L.ldk, bres, rows, n, k, L.ldk, L.n_mod, SC.mm,
+                                R + r0 * L.ldr, L.ldr, 0, d.err, d.num_sms, P.hi, a_plane,
+                                b_plane, r_plane);
+        if (e != cudaSuccess) return e == cudaErrorInvalidValue ? TI_ERR_NO_DEVICE : TI_ERR_CUDA;
+        if (cudaEventRecord(P.gemm_done[b], P.hi) != cudaSuccess) return TI_ERR_CUDA;
+        // lo: split of the next band, then the reconstruction of this one
+        if (b + 1 < bands) {
+            if (split_a(b + 1, P.lo, kSideBlocksPerSm) != cudaSuccess) return TI_ERR_CUDA;
+            if (cudaEventRecord(P.split_done[b + 1], P.lo) != cudaSuccess) return TI_ERR_CUDA;
+        }
+        if (cudaStreamWaitEvent(P.lo, P.gemm_done[b], 0) != cudaSuccess) return TI_ERR_CUDA;
+        if (b == bands - 1) record(ev, 2, P.lo);
+        e = launch_crt(R + r0 * L.ldr, true, L.ldr, r_plane, rows, n, rexp + r0, cexp,
+                       C + r0 * ldc, ldc, out_mode, KC, d.num_sms, P.lo,
+                       b == bands - 1 ? 8 : kSideBlocksPerSm);
+        if (e != cudaSuccess) return TI_ERR_CUDA;
+    }
+    if (cudaEventRecord(P.hi_done, P.hi) != cudaSuccess ||
+        cudaEventRecord(P.lo_done, P.lo) != cudaSuccess ||
+        cudaStreamWaitEvent(s, P.hi_done, 0) != cudaSuccess ||
+        cudaStreamWaitEvent(s, P.lo_done, 0) != cudaSuccess)
+        return TI_ERR_CUDA;
+    record(ev, 3, s);
+    return TI_OK;
+}
+
 int ti_crt_matmul(const double *A, int64_t sa0, int64_t sa1, const double *B, int64_t sb0,
                   int64_t sb1, double *C, int64_t ldc, int64_t m, int64_t n, int64_t k,
                   int bits, int out_mode, void *workspace, size_t workspace_bytes,
@@ -528,6 +653,15 @@ int ti_crt_matmul_ex(const double *A, int64_t sa0, int64_t sa1, const double *B,
     const Plan &PL = L.plan;
     if (!make_split_const(PL.moduli, PL.n_mod, PL.bits, PL.wide, SC)) return TI_ERR_UNSUPPORTED;
     if (!make_crt_const(PL.moduli, PL.n_mod, PL.bits, KC)) return TI_ERR_UNSUPPORTED;
+
+    int bands = opt && opt->bands > 0 ? opt->bands : auto_bands(m);
+    if (bands > kMaxBands) bands = kMaxBands;
+    int64_t band_rows = (m + bands - 1) / bands;
+    band_rows = (band_rows + 127) / 128 * 128;
+    bands = static_cast<int>((m + band_rows - 1) / band_rows);
+    if (bands > 1 && !use_fused(m, n))
+        return crt_matmul_banded(A, sa0, sa1, B, sb0, sb1, C, ldc, m, n, k, out_mode, ev, s, L,
+                                 SC, KC, d, bands, band_rows, rexp, cexp, ares, bres, R);
 
     // K1: A as m vectors along k (rows), B as n vectors along k (columns)
     cudaError_t e;

@@ -105,10 +105,10 @@ template <bool kInU8>
 static cudaError_t launch_crt_t(const void *R, int64_t ldr, int64_t plane, int64_t rows,
                                 int64_t cols, const int32_t *row_exp, const int32_t *col_exp,
                                 double *C, int64_t ldc, int out_mode, const CrtConst &K,
-                                int num_sms, cudaStream_t stream) {
+                                int num_sms, cudaStream_t stream, int blocks_per_sm) {
     const int64_t total = rows * ((cols + 3) >> 2);
     int64_t blocks = (total + 255) / 256;
-    if (blocks > int64_t(num_sms) * 8) blocks = int64_t(num_sms) * 8;
+    if (blocks > int64_t(num_sms) * blocks_per_sm) blocks = int64_t(num_sms) * blocks_per_sm;
     const unsigned g = static_cast<unsigned>(blocks);
     if (out_mode == 0)
         crt_kernel<kInU8, 0><<<g, 256, 0, stream>>>(R, ldr, plane, rows, cols, row_exp, col_exp, C, ldc, K);
@@ -122,13 +122,13 @@ static cudaError_t launch_crt_t(const void *R, int64_t ldr, int64_t plane, int64
 cudaError_t launch_crt(const void *R, bool in_u8, int64_t ldr, int64_t plane, int64_t rows,
                        int64_t cols, const int32_t *row_exp, const int32_t *col_exp, double *C,
                        int64_t ldc, int out_mode, const CrtConst &K, int num_sms,
-                       cudaStream_t stream) {
+                       cudaStream_t stream, int blocks_per_sm) {
     if (rows == 0 || cols == 0) return cudaSuccess;
     if (in_u8)
         return launch_crt_t<true>(R, ldr, plane, rows, cols, row_exp, col_exp, C, ldc, out_mode, K,
-                                  num_sms, stream);
+                                  num_sms, stream, blocks_per_sm);
     return launch_crt_t<false>(R, ldr, plane, rows, cols, row_exp, col_exp, C, ldc, out_mode, K,
-                               num_sms, stream);
+                               num_sms, stream, blocks_per_sm);
 }
 
 }  // namespace ti

@@ -458,12 +458,12 @@ static EncodeTiledFn get_encode_fn() {
 // 3-D map over int8 residue planes [planes][rows][ld] with dims (kdim, rows, planes) and a
 // box of (128, box_rows, 1) using the 128-byte swizzle.
 static bool make_plane_map(CUtensorMap *map, const void *base, int64_t kdim, int64_t rows,
-                           int64_t ld, int64_t planes, int box_rows) {
+                           int64_t ld, int64_t planes, int box_rows, int64_t plane_stride) {
     EncodeTiledFn enc = get_encode_fn();
     if (!enc) return false;
     cuuint64_t dims[3] = {static_cast<cuuint64_t>(kdim), static_cast<cuuint64_t>(rows),
                           static_cast<cuuint64_t>(planes)};
-    cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld), static_cast<cuuint64_t>(ld * rows)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld), static_cast<cuuint64_t>(plane_stride)};
     cuuint32_t box[3] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows), 1};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims,
@@ -486,11 +486,14 @@ static cudaError_t configure(int dev) {
 
 static cudaError_t fill_common(GemmParams &P, CUtensorMap &tmA, CUtensorMap &tmB,
                                const int8_t *a_res, const int8_t *b_res, int64_t m, int64_t n,
-                               int64_t kdim, int64_t ld, int n_mod, const ModMagic &mm, int *err) {
+                               int64_t kdim, int64_t ld, int n_mod, const ModMagic &mm, int *err,
+                               int64_t a_plane, int64_t b_plane) {
     // kdim == 0 is handled by the callers; a map needs at least one column
     const int64_t kd = kdim > 0 ? kdim : 1;
-    if (!make_plane_map(&tmA, a_res, kd, m, ld, n_mod, kBM)) return cudaErrorInvalidValue;
-    if (!make_plane_map(&tmB, b_res, kd, n, ld, n_mod, kBN)) return cudaErrorInvalidValue;
+    if (!make_plane_map(&tmA, a_res, kd, m, ld, n_mod, kBM, a_plane ? a_plane : ld * m))
+        return cudaErrorInvalidValue;
+    if (!make_plane_map(&tmB, b_res, kd, n, ld, n_mod, kBN, b_plane ? b_plane : ld * n))
+        return cudaErrorInvalidValue;
     std::memset(&P, 0, sizeof(P));
     P.m = m;
     P.n = n;
@@ -510,10 +513,14 @@ int gemm_smem_bytes() { return static_cast<int>(kGemmSmemBytes); }
 //   a_res: [n_mod][m][ld] int8, b_res: [n_mod][n][ld] int8 (K-major, ld % 16 == 0)
 //   out:   uint8 [n_mod][m][ldo] (ldo % 16 == 0) or int32 [n_mod][m][ldo]
 // Returns cudaErrorInvalidValue if a tensor map cannot be built.
+// a_plane / b_plane: bytes between the residue planes of A / B (0: ld * m / ld * n);
+// out_plane: elements between output planes (0: m * ldo).  Row bands of larger operands
+// pass their full operands' strides.
 cudaError_t launch_residue_gemm(const int8_t *a_res, const int8_t *b_res, int64_t m, int64_t n,
                                 int64_t kdim, int64_t ld, int n_mod, const ModMagic &mm,
                                 void *out, int64_t ldo, int out_i32, int *err, int num_sms,
-                                cudaStream_t stream) {
+                                cudaStream_t stream, int64_t a_plane, int64_t b_plane,
+                                int64_t out_plane) {
     if (m == 0 || n == 0 || n_mod == 0) return cudaSuccess;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -521,11 +528,11 @@ cudaError_t launch_residue_gemm(const int8_t *a_res, const int8_t *b_res, int64_
     if (e != cudaSuccess) return e;
     CUtensorMap tmA, tmB;
     GemmParams P;
-    e = fill_common(P, tmA, tmB, a_res, b_res, m, n, kdim, ld, n_mod, mm, err);
+    e = fill_common(P, tmA, tmB, a_res, b_res, m, n, kdim, ld, n_mod, mm, err, a_plane, b_plane);
     if (e != cudaSuccess) return e;
     P.out = out;
     P.ldo = ldo;
-    P.plane = m * ldo;
+    P.plane = out_plane ? out_plane : m * ldo;
     P.out_i32 = out_i32;
     const int64_t grid = P.total_units < num_sms ? P.total_units : num_sms;
     residue_gemm_kernel<false><<<static_cast<unsigned>(grid), gemm_threads(false), kGemmSmemBytes,
@@ -557,7 +564,7 @@ cudaError_t launch_fused_gemm_crt(const int8_t *a_res, const int8_t *b_res, int6
     if (e != cudaSuccess) return e;
     CUtensorMap tmA, tmB;
     GemmParams P;
-    e = fill_common(P, tmA, tmB, a_res, b_res, m, n, kdim, ld, K.n_mod, K.mm, err);
+    e = fill_common(P, tmA, tmB, a_res, b_res, m, n, kdim, ld, K.n_mod, K.mm, err, 0, 0);
     if (e != cudaSuccess) return e;
     P.scratch = scratch;
     P.row_exp = row_exp;

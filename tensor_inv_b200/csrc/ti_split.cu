@@ -246,11 +246,16 @@ __global__ void __launch_bounds__(256) split_cols_kernel(
 // ---------------------------------------------------------------------------------------
 // host launchers
 // ---------------------------------------------------------------------------------------
+// plane: bytes between the residue planes of consecutive moduli (0: outer * ld_res, the
+// operand's own planes; a row band of a larger operand passes the full operand's stride).
+// blocks_per_sm caps the grid so the kernel can share SMs with a concurrent GEMM.
 cudaError_t launch_split(const double *X, int64_t outer, int64_t kdim, int64_t s_outer,
                          int64_t s_k, const SplitConst &C, int32_t *exp_out, int8_t *res,
-                         int64_t ld_res, int num_sms, cudaStream_t stream) {
+                         int64_t ld_res, int num_sms, cudaStream_t stream, int64_t plane,
+                         int blocks_per_sm) {
     if (outer == 0) return cudaSuccess;
-    const int64_t plane = outer * ld_res;
+    if (plane == 0) plane = outer * ld_res;
+    const int64_t cap = int64_t(num_sms) * blocks_per_sm;
     if (s_k == 1) {
         const int64_t warps_needed = outer;
         int64_t blocks = (warps_needed + 7) / 8;
@@ -259,7 +264,7 @@ cudaError_t launch_split(const double *X, int64_t outer, int64_t kdim, int64_t s
                                                                            s_outer, exp_out);
         const int64_t total = outer * (ld_res >> 3);
         int64_t sblocks = (total + 255) / 256;
-        if (sblocks > int64_t(num_sms) * 8) sblocks = int64_t(num_sms) * 8;
+        if (sblocks > cap) sblocks = cap;
         if (C.symmetric)
             split_rows_kernel<true><<<static_cast<unsigned>(sblocks), 256, 0, stream>>>(
                 X, outer, kdim, s_outer, exp_out, res, ld_res, plane, C);
@@ -273,7 +278,7 @@ cudaError_t launch_split(const double *X, int64_t outer, int64_t kdim, int64_t s
         const int64_t tiles = ((outer + kColTileO - 1) / kColTileO) *
                               ((ld_res + kColTileK - 1) / kColTileK);
         int64_t sblocks = tiles;
-        if (sblocks > int64_t(num_sms) * 8) sblocks = int64_t(num_sms) * 8;
+        if (sblocks > cap) sblocks = cap;
         if (C.symmetric)
             split_cols_kernel<true><<<static_cast<unsigned>(sblocks), 256, 0, stream>>>(
                 X, outer, kdim, s_k, exp_out, res, ld_res, plane, C);

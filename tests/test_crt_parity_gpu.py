@@ -7,6 +7,7 @@ column exponents only on B's columns, so every output block of the full product 
 the product of the matching panels).
 """
 
+import ctypes
 import importlib
 
 import numpy as np
@@ -381,3 +382,60 @@ def test_moduli_errors(ti):
     with pytest.raises(ValueError):
         big = torch.zeros(1, 133145, dtype=torch.float64, device="cuda")
         ti.crt_matmul(big, big.T, moduli="wide")
+
+
+# ---------------------------------------------------------------------------------------
+# banded pipeline (row bands over two internal streams) against one in-order band
+# ---------------------------------------------------------------------------------------
+def _run_ex(A, B, C, out_mode, bands, moduli=None):
+    from tensor_inv_b200 import _native as nat
+
+    m, k = A.shape
+    n = B.shape[1]
+    opt = nat.options(moduli, None, None, bands)
+    ws_bytes = nat.crt_workspace_size_ex(m, n, k, 53, opt)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    st = nat.lib().ti_crt_matmul_ex(A.data_ptr(), A.stride(0), A.stride(1), B.data_ptr(),
+                                    B.stride(0), B.stride(1), C.data_ptr(), C.stride(0), m, n, k,
+                                    53, out_mode, ws.data_ptr(), ws_bytes,
+                                    torch.cuda.current_stream().cuda_stream, ctypes.byref(opt))
+    nat.check("ti_crt_matmul_ex", st)
+    return C
+
+
+@pytest.mark.parametrize("moduli", [None, "wide"])
+def test_banded_pipeline_matches_single_band(ti, oracle, moduli):
+    m, n, k = 2500, 700, 1500   # 3 bands of 896, 896 and 708 rows
+    A = _rand((m, k), 101, 1.0).cuda()
+    B = _rand((n, k), 102, 1.0).T.cuda()      # transposed view: column split path
+    C1 = _run_ex(A, B, torch.empty(m, n, dtype=torch.float64, device="cuda"), 0, 1, moduli)
+    for bands in (2, 3, 8):
+        Cb = _run_ex(A, B, torch.full((m, n), float("nan"), dtype=torch.float64, device="cuda"),
+                     0, bands, moduli)
+        _assert_bitexact(Cb, C1.cpu().numpy())
+    want = oracle.crt_matmul(A[2400:2500].cpu().numpy(), B[:, 600:700].cpu().numpy(), 53)
+    _assert_bitexact(C1[2400:2500, 600:700], want)
+
+
+def test_banded_update_mode(ti, oracle):
+    m, n, k = 2100, 300, 256
+    A = _rand((m, k), 111)
+    B = _rand((k, n), 112)
+    C0 = _rand((m, n), 113)
+    want = C0.numpy() - oracle.crt_matmul(A.numpy(), B.numpy(), 53)
+    C = _run_ex(A.cuda(), B.cuda(), C0.cuda(), 1, 4)
+    _assert_bitexact(C, want)
+
+
+def test_banded_on_side_stream(ti, oracle):
+    """The pipeline forks from and joins back to the caller's (non-default) stream."""
+    m, n, k = 4096, 512, 700
+    A = _rand((m, k), 121).cuda()
+    B = _rand((k, n), 122).cuda()
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        C = ti.crt_matmul(A, B)
+        D = C * 1.0   # consumer on the same stream must see the finished product
+    s.synchronize()
+    want = oracle.crt_matmul(A[:64].cpu().numpy(), B.cpu().numpy(), 53)
+    _assert_bitexact(D[:64], want)
