@@ -172,6 +172,25 @@ int ti_crt_matmul_ex(const double *A, int64_t sa0, int64_t sa1, const double *B,
                      void *stream, const ti_crt_options_t *opt);
 
 /*
+ * crt_matmul on HOST operands (the reference's CPU-tensor call, crt_matmul.py:101), with
+ * the copies pipelined against the kernels: all of B goes to the device first, then A in
+ * row bands; each band is split, multiplied and reconstructed on `stream` as soon as it has
+ * arrived, and its rows of C are copied back while the next band computes.  The three copy
+ * streams run on the copy engines, so the transfers overlap the kernels.  Host memory
+ * should be pinned (page-locked) for the copies to overlap; pageable memory still works,
+ * serially.  A (m x k) element (i,l) at A[i*sa0 + l*sa1], B (k x n) at B[l*sb0 + j*sb1] (one
+ * stride of each 1); C row-major host, leading dimension ldc; C = A @ B (store).  The call
+ * is asynchronous on `stream`: synchronize it before reading C.
+ * workspace: device scratch of ti_crt_host_workspace_size() bytes, 256-byte aligned.
+ */
+int ti_crt_host_workspace_size(int64_t m, int64_t n, int64_t k, int bits,
+                               const ti_crt_options_t *opt, size_t *bytes);
+int ti_crt_matmul_host(const double *A, int64_t sa0, int64_t sa1, const double *B, int64_t sb0,
+                       int64_t sb1, double *C, int64_t ldc, int64_t m, int64_t n, int64_t k,
+                       int bits, void *workspace, size_t workspace_bytes, void *stream,
+                       const ti_crt_options_t *opt);
+
+/*
  * ti_crt_matmul that also records four caller-created CUDA events (cudaEvent_t, passed as
  * void*; NULL entries are skipped) on `stream`: stage_events[0] before K1 (split),
  * [1] before K2 (residue GEMM), [2] before K3 (CRT), [3] after K3.  For profiling; the

@@ -65,6 +65,9 @@ SIGNATURES = {
     "ti_crt_workspace_size_ex": (_int, [_i64, _i64, _i64, _int, _opt, ctypes.POINTER(_sz)]),
     "ti_crt_matmul_ex": (_int, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i64, _i64, _int,
                                 _int, _p, _sz, _p, _opt]),
+    "ti_crt_host_workspace_size": (_int, [_i64, _i64, _i64, _int, _opt, ctypes.POINTER(_sz)]),
+    "ti_crt_matmul_host": (_int, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i64, _i64,
+                                  _int, _p, _sz, _p, _opt]),
     "ti_device_error": (_int, [ctypes.POINTER(_int), _int]),
 }
 
@@ -179,4 +182,11 @@ def batched_gemm_workspace_size(batch: int, M: int, K: int, N: int) -> int:
 def device_error(reset: bool = True) -> int:
     out = ctypes.c_int(0)
     check("ti_device_error", lib().ti_device_error(ctypes.byref(out), 1 if reset else 0))
+    return out.value
+
+
+def crt_host_workspace_size(m: int, n: int, k: int, bits: int, opt: CrtOptions) -> int:
+    out = ctypes.c_size_t(0)
+    check("ti_crt_host_workspace_size",
+          lib().ti_crt_host_workspace_size(m, n, k, bits, ctypes.byref(opt), ctypes.byref(out)))
     return out.value

@@ -152,6 +152,8 @@ def crt_matmul(A, B, *, moduli=None, n_moduli=None):
     n = B.shape[1]
     home = A.device
     dev = _cuda_device(A, B)
+    if home.type == "cpu" and B.device.type == "cpu":
+        return _crt_matmul_host(A.to(torch.float64), B.to(torch.float64), bits, opt, dev)
     A = A.to(device=dev, dtype=torch.float64)
     B = B.to(device=dev, dtype=torch.float64)
     C = torch.empty((m, n), dtype=torch.float64, device=dev)
@@ -165,6 +167,77 @@ def crt_matmul(A, B, *, moduli=None, n_moduli=None):
         out.copy_(C)
         return out
     return C.to(home)
+
+
+class _PinnedPool:
+    """Reusable page-locked host blocks for results returned on the CPU.
+
+    A fresh 512 MiB pinned allocation costs ~64 ms on a B200 host (more than the product
+    itself) whenever the previous result is still alive, which is the common loop
+    ``C = crt_matmul(A, B)``.  Each result is a view of a pooled block; a block is handed
+    out again only when no tensor, view or numpy array refers to its storage any more
+    (storage use count back to the pool's own references), so a live result is never
+    overwritten.  Blocks beyond ``max_bytes`` in total are not pooled.
+    """
+
+    def __init__(self, max_bytes=8 << 30):
+        import threading
+
+        self._lock = threading.Lock()
+        self._blocks = []
+        self._max = max_bytes
+        self._count = getattr(torch._C, "_storage_Use_Count", None)
+
+    def _free(self, base):
+        # references: the pool's tensor plus the temporary storage wrapper of this call
+        return self._count(base.untyped_storage()._cdata) <= 2
+
+    def empty(self, m, n):
+        nbytes = 8 * m * n
+        if self._count is None or nbytes == 0:
+            return torch.empty((m, n), dtype=torch.float64, pin_memory=True)
+        with self._lock:
+            best = None
+            for base in self._blocks:
+                if base.numel() >= nbytes and self._free(base):
+                    if best is None or base.numel() < best.numel():
+                        best = base
+            if best is None:
+                best = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+                if sum(b.numel() for b in self._blocks) + nbytes <= self._max:
+                    self._blocks.append(best)
+            return best[:nbytes].view(torch.float64).view(m, n)
+
+
+_pinned_pool = _PinnedPool()
+
+
+def _crt_matmul_host(A, B, bits, opt, dev):
+    """CPU operands: copies and kernels pipelined in row bands (ti_crt_matmul_host); the
+    result lands in pinned host memory.  Synchronous, like the reference's CPU call."""
+    m, k = A.shape
+    n = B.shape[1]
+    sa = _strides_2d(A)
+    if sa is None:
+        A = A.contiguous()
+        sa = A.stride()
+    sb = _strides_2d(B)
+    if sb is None:
+        B = B.contiguous()
+        sb = B.stride()
+    out = _pinned_pool.empty(m, n)
+    if m == 0 or n == 0:
+        return out
+    ws_bytes = nat.crt_host_workspace_size(m, n, k, bits, opt)
+    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev)
+        st = nat.lib().ti_crt_matmul_host(
+            A.data_ptr(), sa[0], sa[1], B.data_ptr(), sb[0], sb[1], out.data_ptr(), n, m, n, k,
+            bits, ws.data_ptr(), ws.numel(), stream.cuda_stream, ctypes.byref(opt))
+        nat.check("ti_crt_matmul_host", st)
+        stream.synchronize()  # A, B and the workspace stay alive until the copies are done
+    return out
 
 
 def crt_matmul_update(C, A, B, alpha=-1, *, moduli=None, n_moduli=None):

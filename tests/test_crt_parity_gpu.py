@@ -439,3 +439,57 @@ def test_banded_on_side_stream(ti, oracle):
     s.synchronize()
     want = oracle.crt_matmul(A[:64].cpu().numpy(), B.cpu().numpy(), 53)
     _assert_bitexact(D[:64], want)
+
+
+# ---------------------------------------------------------------------------------------
+# host operands: copies pipelined with the kernels (ti_crt_matmul_host)
+# ---------------------------------------------------------------------------------------
+@pytest.mark.parametrize("pinned", [True, False])
+@pytest.mark.parametrize("moduli", [None, "wide"])
+def test_host_pipeline_matches_device_path(ti, pinned, moduli):
+    m, n, k = 2500, 333, 1100   # 4 bands of 640 rows (the last 580)
+    A = _rand((m, k), 131, 1.0)
+    B = _rand((k, n), 132, 1.0)
+    if pinned:
+        A, B = A.pin_memory(), B.pin_memory()
+    C = ti.crt_matmul(A, B, moduli=moduli)
+    assert C.device.type == "cpu" and C.shape == (m, n)
+    want = ti.crt_matmul(A.cuda(), B.cuda(), moduli=moduli)
+    _assert_bitexact(C, want.cpu().numpy())
+
+
+def test_host_pipeline_transposed_views(ti, oracle):
+    A = _rand((300, 900), 141, 0.5).T     # 900 x 300, column-major view
+    B = _rand((250, 300), 142, 0.5).T     # 300 x 250, column-major view
+    want = oracle.crt_matmul(A.numpy(), B.numpy(), 53)
+    _assert_bitexact(ti.crt_matmul(A, B), want)
+
+
+def test_host_results_are_never_overwritten(ti):
+    """Results returned on the CPU come from a pool of pinned blocks; a block still referred
+    to (by the result, a view of it or a numpy array) must not be handed out again."""
+    A = _rand((300, 200), 151)
+    B = _rand((200, 100), 152)
+    C1 = ti.crt_matmul(A, B)
+    keep_view = C1[10:20]
+    keep_np = C1.numpy()
+    snap = C1.clone()
+    del C1
+    C2 = ti.crt_matmul(2 * A, B)
+    assert C2.data_ptr() != keep_view.data_ptr() - 10 * 100 * 8
+    assert torch.equal(keep_view, snap[10:20])
+    del keep_view
+    assert np.array_equal(keep_np, snap.numpy())
+    assert torch.equal(C2, ti.crt_matmul((2 * A).cuda(), B.cuda()).cpu())
+
+
+def test_host_result_blocks_are_reused(ti):
+    """Dropped results give their pinned block back: steady state allocates nothing."""
+    A = _rand((256, 128), 161)
+    B = _rand((128, 64), 162)
+    ptrs = set()
+    C = None
+    for _ in range(6):
+        C = ti.crt_matmul(A, B)   # the previous result dies when C is rebound
+        ptrs.add(C.data_ptr())
+    assert len(ptrs) <= 2
