@@ -1,0 +1,91 @@
+"""2-D sharded CRT matmul on world_size 2 and 4 gloo ranks (CPU, no GPU).
+
+The block compute is the CPU oracle here (the product itself needs a B200); what is under
+test is the sharding: block ranges, the panel broadcasts from one rank, the no-collective
+block product, and the all-gather of C, which must reproduce the single-process result
+bit for bit.
+"""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, m, n, k, out_q):
+    import torch.distributed as dist
+
+    from oracle import oracle
+    from tensor_inv_b200 import distributed as D
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        A = B = None
+        if rank == 0:
+            g = torch.Generator().manual_seed(5)
+            A = torch.randn(m, k, generator=g, dtype=torch.float64)
+            B = torch.randn(k, n, generator=g, dtype=torch.float64) * 1e3
+        Ap, Bp = D.scatter_panels(A, B, m, n, k, src=0)
+        (r0, r1), (c0, c1) = D.my_ranges(m, n, rank, world)
+        assert Ap.shape == (r1 - r0, k) and Bp.shape == (k, c1 - c0)
+        Cb = D.crt_matmul_2d(Ap, Bp, matmul=lambda a, b: torch.from_numpy(
+            oracle.crt_matmul(a.numpy(), b.numpy(), 53)))
+        C = D.gather_blocks(Cb, m, n)
+        if rank == 0:
+            out_q.put(C.numpy().copy())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_sharded_matches_single_process(oracle, world):
+    m, n, k = 300, 270, 90
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, m, n, k, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        C = q.get(timeout=120)  # read before joining: a child that queued data exits only
+    finally:                    # once its data has been read
+        for p in procs:
+            p.join(timeout=60)
+        codes = [p.exitcode for p in procs]
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+    assert codes == [0] * world, codes
+    g = torch.Generator().manual_seed(5)
+    A = torch.randn(m, k, generator=g, dtype=torch.float64)
+    B = torch.randn(k, n, generator=g, dtype=torch.float64) * 1e3
+    want = oracle.crt_matmul(A.numpy(), B.numpy(), 53)
+    assert np.array_equal(C.view(np.uint64), want.view(np.uint64))
+
+
+def test_grid_and_ranges():
+    from tensor_inv_b200 import distributed as D
+
+    assert [D.grid_shape(w) for w in (1, 2, 4, 8, 6, 9)] == [(1, 1), (1, 2), (2, 2), (2, 4),
+                                                            (2, 3), (3, 3)]
+    for size, parts in [(8192, 2), (8192, 4), (1000, 3), (100, 4), (5, 8)]:
+        cuts = [D.block_range(size, parts, i) for i in range(parts)]
+        assert cuts[0][0] == 0 and cuts[-1][1] == size
+        assert all(a[1] == b[0] for a, b in zip(cuts, cuts[1:]))
+        assert all(c[0] % 128 == 0 for c in cuts if c[0] < size)
+    covered = np.zeros((1000, 700), int)
+    for r in range(8):
+        (r0, r1), (c0, c1) = D.my_ranges(1000, 700, r, 8)
+        covered[r0:r1, c0:c1] += 1
+    assert (covered == 1).all()
