@@ -426,11 +426,12 @@ def run_ours(args):
     bf16 = None
     if peaks_file.exists():
         bf16 = json.loads(peaks_file.read_text()).get("bf16_tflops")
+    # only rank 0 prints, so only rank 0 measures the cuBLAS int8 reference
     int8_cublas = measure_int8_peak(torch, dev) if rank == 0 else None
     cands = [x for x in (int8_cublas, 2 * bf16 if bf16 else None) if x]
     peak = max(cands) if cands else 4500.0
     peak_src = ("max(cuBLAS int8 8192^3 burst measured in this run = "
-                f"{int8_cublas:.0f}, 2 x measured bf16 dense {bf16} = "
+                f"{int8_cublas or float('nan'):.0f}, 2 x measured bf16 dense {bf16} = "
                 f"{2 * bf16 if bf16 else float('nan'):.0f}) tera-ops/s" if cands else
                 "fallback: datasheet 4500 dense int8 tera-ops/s")
     gemm_ops = 2.0 * m * n * k * n_mod
