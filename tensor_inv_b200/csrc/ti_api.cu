@@ -19,7 +19,7 @@ cudaError_t launch_residue_gemm(const int8_t *a_res, const int8_t *b_res, int64_
                                 int64_t kdim, int64_t ld, int n_mod, const ModMagic &mm,
                                 void *out, int64_t ldo, int out_i32, int *err, int num_sms,
                                 cudaStream_t stream, int64_t a_plane = 0, int64_t b_plane = 0,
-                                int64_t out_plane = 0);
+                                int64_t out_plane = 0, const uint32_t *weights = nullptr);
 cudaError_t launch_crt(const void *R, bool in_u8, int64_t ldr, int64_t plane, int64_t rows,
                        int64_t cols, const int32_t *row_exp, const int32_t *col_exp, double *C,
                        int64_t ldc, int out_mode, const CrtConst &K, int num_sms,
@@ -192,6 +192,7 @@ static bool make_split_const(const int32_t *moduli, int n_mod, int bits, bool sy
         C.w32[i] = static_cast<uint32_t>((uint64_t(1) << 32) % p);
         C.w16[i] = static_cast<uint32_t>((uint64_t(1) << 16) % p);
         C.bigp[i] = static_cast<uint32_t>(p * (((uint64_t(1) << 29) + p - 1) / p));
+        C.offs[i] = static_cast<uint32_t>(p * ((uint64_t(549388288) + p - 1) / p));
     }
     return true;
 }
@@ -228,6 +229,19 @@ static bool make_crt_const(const int32_t *moduli, int n_mod, int bits, CrtConst 
     for (int w = 0; w < 4; ++w) {
         K.M[w] = static_cast<uint32_t>(M >> (32 * w));
         K.H[w] = static_cast<uint32_t>(H >> (32 * w));
+    }
+    // groups of three consecutive moduli (P_g <= 255^3 < 2^24, so c_g < 3 P_g < 2^26)
+    K.n_groups = (n_mod + 2) / 3;
+    for (int g = 0; g < K.n_groups; ++g) {
+        uint64_t Pg = 1;
+        for (int i = 3 * g; i < 3 * g + 3 && i < n_mod; ++i) Pg *= static_cast<uint32_t>(moduli[i]);
+        for (int i = 3 * g; i < 3 * g + 3 && i < n_mod; ++i)
+            K.coef[i] = static_cast<uint32_t>(Pg / static_cast<uint32_t>(moduli[i]));
+        const u128 Mg = M / Pg;
+        for (int w = 0; w < 4; ++w) K.Mg[g][w] = static_cast<uint32_t>(Mg >> (32 * w));
+        const uint64_t finv = ((uint64_t(1) << 48) + Pg / 2) / Pg;  // round(2^48 / P_g)
+        K.fgl[g] = static_cast<uint32_t>(finv);
+        K.fgh[g] = static_cast<uint32_t>(finv >> 32);
     }
     return true;
 }
@@ -584,7 +598,7 @@ static int crt_matmul_banded(const double *A, int64_t sa0, int64_t sa1, const do
             return TI_ERR_CUDA;
         e = launch_residue_gemm(ares + r0 * L.ldk, bres, rows, n, k, L.ldk, L.n_mod, SC.mm,
                                 R + r0 * L.ldr, L.ldr, 0, d.err, d.num_sms, P.hi, a_plane,
-                                b_plane, r_plane);
+                                b_plane, r_plane, KC.u);
         if (e != cudaSuccess) return e == cudaErrorInvalidValue ? TI_ERR_NO_DEVICE : TI_ERR_CUDA;
         if (cudaEventRecord(P.gemm_done[b], P.hi) != cudaSuccess) return TI_ERR_CUDA;
         // lo: split of the next band, then the reconstruction of this one
@@ -660,7 +674,10 @@ int ti_crt_matmul_ex(const double *A, int64_t sa0, int64_t sa1, const double *B,
     SplitConst SC;
     CrtConst KC;
     const Plan &PL = L.plan;
-    if (!make_split_const(PL.moduli, PL.n_mod, PL.bits, PL.wide, SC)) return TI_ERR_UNSUPPORTED;
+    // symmetric residues on the matmul path for either moduli set: the residue products
+    // mod p do not depend on the representative (the stage entry ti_crt_split keeps the
+    // reference's floor-mod bytes)
+    if (!make_split_const(PL.moduli, PL.n_mod, PL.bits, true, SC)) return TI_ERR_UNSUPPORTED;
     if (!make_crt_const(PL.moduli, PL.n_mod, PL.bits, KC)) return TI_ERR_UNSUPPORTED;
 
     int bands = opt && opt->bands > 0 ? opt->bands : auto_bands(m);
@@ -696,7 +713,7 @@ int ti_crt_matmul_ex(const double *A, int64_t sa0, int64_t sa1, const double *B,
     }
     // K2: per-modulus residue GEMMs, mod-reduced to uint8 planes
     e = launch_residue_gemm(ares, bres, m, n, k, L.ldk, L.n_mod, SC.mm, R, L.ldr, 0, d.err,
-                            d.num_sms, s);
+                            d.num_sms, s, 0, 0, 0, KC.u);
     if (e != cudaSuccess) return e == cudaErrorInvalidValue ? TI_ERR_NO_DEVICE : TI_ERR_CUDA;
     // K3: exact CRT + inverse scaling
     record(ev, 2, s);
@@ -731,7 +748,7 @@ static int crt_band_compute(const double *A, int64_t sa0, int64_t sa1, const dou
     else e = launch_split(A, rows, k, 1, sa1, SC, rexp, ares, L.ldk, d.num_sms, s);
     if (e != cudaSuccess) return TI_ERR_CUDA;
     e = launch_residue_gemm(ares, bres, rows, n, k, L.ldk, L.n_mod, SC.mm, R, L.ldr, 0, d.err,
-                            d.num_sms, s);
+                            d.num_sms, s, 0, 0, 0, KC.u);
     if (e != cudaSuccess) return e == cudaErrorInvalidValue ? TI_ERR_NO_DEVICE : TI_ERR_CUDA;
     e = launch_crt(R, true, L.ldr, rows * L.ldr, rows, n, rexp, cexp, C, ldc, TI_OUT_STORE, KC,
                    d.num_sms, s);
@@ -799,7 +816,7 @@ int ti_crt_matmul_host(const double *A, int64_t sa0, int64_t sa1, const double *
     SplitConst SC;
     CrtConst KC;
     if (k > 0) {
-        if (!make_split_const(L.plan.moduli, L.plan.n_mod, L.plan.bits, L.plan.wide, SC) ||
+        if (!make_split_const(L.plan.moduli, L.plan.n_mod, L.plan.bits, true, SC) ||
             !make_crt_const(L.plan.moduli, L.plan.n_mod, L.plan.bits, KC))
             return TI_ERR_UNSUPPORTED;
     }

@@ -62,6 +62,8 @@ struct SplitConst {
     uint32_t w32[kMaxModuli];   // 2^32 mod p
     uint32_t w16[kMaxModuli];   // 2^16 mod p
     uint32_t bigp[kMaxModuli];  // p * ceil(2^29 / p): a multiple of p that is >= 2^29
+    uint32_t offs[kMaxModuli];  // p * ceil(549388288 / p): a multiple of p above any |T|
+                                // (T = a2*w32 + a1*w16 + a0 of signed pieces, |T| < 549388288)
 };
 
 // Constants of the CRT reconstruction.  M = prod p_i < 2^127, M_i = M / p_i.
@@ -74,6 +76,14 @@ struct CrtConst {
     uint32_t Mi[kMaxModuli][4];    // M_i, little-endian 32-bit words
     uint32_t M[4];
     uint32_t H[4];                 // (M - 1) / 2
+    // Moduli in groups of (up to) three consecutive ones, g = i / 3: with P_g the product of
+    // a group, c_g = sum_{i in g} t_i * (P_g / p_i) < 3 P_g < 2^26, and
+    //   S = sum_g c_g * (M / P_g),   F = sum_g c_g / P_g   (48-bit fixed point)
+    // which equal the per-modulus sums with a third of the 128-bit multiply-adds.
+    int n_groups;
+    uint32_t coef[kMaxModuli];     // P_g / p_i for the group g of modulus i
+    uint32_t Mg[kMaxModuli / 3 + 1][4];
+    uint32_t fgl[kMaxModuli / 3 + 1], fgh[kMaxModuli / 3 + 1];  // round(2^48 / P_g), lo/hi words
 };
 
 // ---------------------------------------------------------------------------------------

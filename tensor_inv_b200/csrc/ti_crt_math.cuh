@@ -99,7 +99,9 @@ __device__ __forceinline__ void lift_symmetric(uint32_t &w0, uint32_t &w1, uint3
     }
 }
 
-// One element: column sums s0..s3 of S, fixed-point F, exponent sum e2 = re + ce - 2*bits.
+// One element: column sums s0..s3 of S, F = S / M in fixed point with kFracBits fraction
+// bits, exponent sum e2 = re + ce - 2*bits.
+template <int kFracBits = 32>
 __device__ __forceinline__ double crt_finish(uint64_t s0, uint64_t s1, uint64_t s2, uint64_t s3,
                                              uint64_t f, int e2, const CrtConst &K) {
     // carry-propagate the four 64-bit column sums into 128 bits
@@ -112,7 +114,7 @@ __device__ __forceinline__ double crt_finish(uint64_t s0, uint64_t s1, uint64_t 
     c = (c >> 32) + s3;
     uint32_t w3 = static_cast<uint32_t>(c);
     // x = S - q*M  (mod 2^128)
-    const uint32_t qv = static_cast<uint32_t>((f + 0x80000000ull) >> 32);
+    const uint32_t qv = static_cast<uint32_t>((f + (1ull << (kFracBits - 1))) >> kFracBits);
     uint64_t b = static_cast<uint64_t>(qv) * K.M[0];
     uint64_t d = static_cast<uint64_t>(w0) - static_cast<uint32_t>(b);
     w0 = static_cast<uint32_t>(d);

@@ -55,6 +55,7 @@ struct GemmParams {
     int64_t ldo;       // elements; multiple of 16 for uint8 output
     int64_t plane;     // elements between moduli planes
     int out_i32;       // 0: uint8 residues (|accumulator| <= 2^31 - 256); 1: int32, any int8
+    int store_t;       // uint8 output holds t = (r * crt.u[i]) mod p instead of r
     // fused output
     uint8_t *scratch;  // 2 slots x n_mod x 128 x 256 bytes per CTA
     const int32_t *row_exp, *col_exp;
@@ -369,12 +370,15 @@ __global__ void __launch_bounds__(gemm_threads(kFused), 1)
                 } else if (row < P.m && col0 < P.ldo) {
                     if (!P.out_i32) {
                         uint32_t pk[8];
+                        const uint32_t wt = P.store_t ? P.crt.u[mod] : 1u;
 #pragma unroll
                         for (int j = 0; j < 8; ++j) {
                             uint32_t w = 0;
 #pragma unroll
-                            for (int b = 0; b < 4; ++b)
-                                w |= mod_acc(v[4 * j + b], p, magic, shift, off) << (8 * b);
+                            for (int b = 0; b < 4; ++b) {
+                                const uint32_t r = mod_acc(v[4 * j + b], p, magic, shift, off);
+                                w |= mod_small(r * wt, p, magic, shift) << (8 * b);
+                            }
                             pk[j] = w;
                         }
                         uint8_t *dst = static_cast<uint8_t *>(P.out) + mod * P.plane + row * P.ldo + col0;
@@ -516,11 +520,12 @@ int gemm_smem_bytes() { return static_cast<int>(kGemmSmemBytes); }
 // a_plane / b_plane: bytes between the residue planes of A / B (0: ld * m / ld * n);
 // out_plane: elements between output planes (0: m * ldo).  Row bands of larger operands
 // pass their full operands' strides.
+// weights: if not null, the uint8 output holds t_i = (r_i * weights[i]) mod p_i.
 cudaError_t launch_residue_gemm(const int8_t *a_res, const int8_t *b_res, int64_t m, int64_t n,
                                 int64_t kdim, int64_t ld, int n_mod, const ModMagic &mm,
                                 void *out, int64_t ldo, int out_i32, int *err, int num_sms,
                                 cudaStream_t stream, int64_t a_plane, int64_t b_plane,
-                                int64_t out_plane) {
+                                int64_t out_plane, const uint32_t *weights) {
     if (m == 0 || n == 0 || n_mod == 0) return cudaSuccess;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -534,6 +539,10 @@ cudaError_t launch_residue_gemm(const int8_t *a_res, const int8_t *b_res, int64_
     P.ldo = ldo;
     P.plane = out_plane ? out_plane : m * ldo;
     P.out_i32 = out_i32;
+    if (weights && !out_i32) {
+        P.store_t = 1;
+        for (int i = 0; i < n_mod; ++i) P.crt.u[i] = weights[i];
+    }
     const int64_t grid = P.total_units < num_sms ? P.total_units : num_sms;
     residue_gemm_kernel<false><<<static_cast<unsigned>(grid), gemm_threads(false), kGemmSmemBytes,
                                  stream>>>(tmA, tmB, P);

@@ -53,8 +53,7 @@ __device__ __forceinline__ uint64_t scaled_magnitude(double x, int bits, int e, 
 }
 
 // Residue bytes of 8 signed values (magnitudes mag[j] < 2^53, signs neg[j]) mod p_i,
-// packed little-endian into two 32-bit words.  kSym selects symmetric residues.
-template <bool kSym>
+// packed little-endian into two 32-bit words: floor-mod residues in [0, p).
 __device__ __forceinline__ uint2 residues8(const uint32_t (&a2)[8], const uint32_t (&a1)[8],
                                            const uint32_t (&a0)[8], uint32_t negmask,
                                            const SplitConst &C, int i) {
@@ -65,19 +64,47 @@ __device__ __forceinline__ uint2 residues8(const uint32_t (&a2)[8], const uint32
     for (int j = 0; j < 8; ++j) {
         // mag = a2*2^32 + a1*2^16 + a0  ==>  t == mag (mod p), t < 2^29
         uint32_t t = a2[j] * w32 + a1[j] * w16 + a0[j];
-        uint32_t r;
-        if (!kSym) {
-            t = ((negmask >> j) & 1u) ? bigp - t : t;  // -mag (mod p), still < 2^30
-            r = mod_small(t, p, magic, shift);
-        } else {
-            int32_t rs = static_cast<int32_t>(mod_small(t, p, magic, shift));
-            rs = rs > static_cast<int32_t>(p >> 1) ? rs - static_cast<int32_t>(p) : rs;
-            rs = ((negmask >> j) & 1u) ? -rs : rs;
-            r = static_cast<uint32_t>(rs) & 0xFFu;
-        }
+        t = ((negmask >> j) & 1u) ? bigp - t : t;  // -mag (mod p), still < 2^30
+        const uint32_t r = mod_small(t, p, magic, shift);
         out[j >> 2] |= r << (8 * (j & 3));
     }
     return make_uint2(out[0], out[1]);
+}
+
+// Symmetric residues of 8 signed values given as signed pieces (v = a2*2^32 + a1*2^16 + a0
+// with every piece carrying the sign of v): T = a2*w32 + a1*w16 + a0 == v (mod p) with
+// |T| < 549388288; u = T + offs (a multiple of p above |T|, so 0 <= u < 2^31);
+// q = floor((u + h) / p) exactly, and u - q*p is the residue in [-h, h], h = (p-1)/2.
+__device__ __forceinline__ uint2 residues8_sym(const uint32_t (&a2)[8], const uint32_t (&a1)[8],
+                                               const uint32_t (&a0)[8], const SplitConst &C,
+                                               int i) {
+    const uint32_t p = C.mm.p[i], magic = C.mm.magic[i], shift = C.mm.shift[i];
+    const uint32_t w32 = C.w32[i], w16 = C.w16[i], offs = C.offs[i], h = p >> 1;
+    uint32_t r[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const uint32_t u = a2[j] * w32 + a1[j] * w16 + (a0[j] + offs);
+        const uint32_t q = __umulhi(u + h, magic) >> shift;
+        r[j] = u - q * p;  // low byte is the two's-complement residue
+    }
+    const uint32_t lo = __byte_perm(__byte_perm(r[0], r[1], 0x0040), __byte_perm(r[2], r[3], 0x0040),
+                                    0x5410);
+    const uint32_t hi = __byte_perm(__byte_perm(r[4], r[5], 0x0040), __byte_perm(r[6], r[7], 0x0040),
+                                    0x5410);
+    return make_uint2(lo, hi);
+}
+
+// Negate the pieces of negative values (two's complement), once per element.
+__device__ __forceinline__ void sign_pieces(uint32_t (&a2)[8], uint32_t (&a1)[8],
+                                            uint32_t (&a0)[8], uint32_t negmask) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        if ((negmask >> j) & 1u) {
+            a2[j] = 0u - a2[j];
+            a1[j] = 0u - a1[j];
+            a0[j] = 0u - a0[j];
+        }
+    }
 }
 
 __device__ __forceinline__ void decompose8(const double (&x)[8], int bits, int e,
@@ -160,12 +187,12 @@ __global__ void __launch_bounds__(256) split_rows_kernel(
     const int32_t *__restrict__ exps, int8_t *__restrict__ res, int64_t ld_res,
     int64_t plane, const __grid_constant__ SplitConst C) {
     const int64_t chunks_per_vec = ld_res >> 3;
-    const int64_t total = outer * chunks_per_vec;
     const bool vec_ok = ((reinterpret_cast<uintptr_t>(X) & 15) == 0) && ((s_outer & 1) == 0);
-    for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
-         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t o = idx / chunks_per_vec;
-        const int64_t l0 = (idx - o * chunks_per_vec) << 3;
+    // vectors by blockIdx.y, 8-element chunks of a vector by blockIdx.x (no division)
+    for (int64_t o = blockIdx.y; o < outer; o += gridDim.y)
+    for (int64_t ch = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+         ch < chunks_per_vec; ch += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t l0 = ch << 3;
         const double *x = X + o * s_outer + l0;
         double v[8];
         if (vec_ok && l0 + 8 <= kdim) {
@@ -183,8 +210,10 @@ __global__ void __launch_bounds__(256) split_rows_kernel(
         uint32_t a2[8], a1[8], a0[8], negmask;
         decompose8(v, C.bits, e, a2, a1, a0, negmask);
         int8_t *dst = res + o * ld_res + l0;
+        if (kSym) sign_pieces(a2, a1, a0, negmask);
         for (int i = 0; i < C.n_mod; ++i) {
-            const uint2 w = residues8<kSym>(a2, a1, a0, negmask, C, i);
+            const uint2 w = kSym ? residues8_sym(a2, a1, a0, C, i)
+                                 : residues8(a2, a1, a0, negmask, C, i);
             *reinterpret_cast<uint2 *>(dst + i * plane) = w;
         }
     }
@@ -234,8 +263,10 @@ __global__ void __launch_bounds__(256) split_cols_kernel(
             uint32_t a2[8], a1[8], a0[8], negmask;
             decompose8(v, C.bits, e, a2, a1, a0, negmask);
             int8_t *dst = res + o * ld_res + lc;
+            if (kSym) sign_pieces(a2, a1, a0, negmask);
             for (int i = 0; i < C.n_mod; ++i) {
-                const uint2 w = residues8<kSym>(a2, a1, a0, negmask, C, i);
+                const uint2 w = kSym ? residues8_sym(a2, a1, a0, C, i)
+                                     : residues8(a2, a1, a0, negmask, C, i);
                 *reinterpret_cast<uint2 *>(dst + i * plane) = w;
             }
         }
@@ -262,15 +293,20 @@ cudaError_t launch_split(const double *X, int64_t outer, int64_t kdim, int64_t s
         if (blocks > int64_t(num_sms) * 16) blocks = int64_t(num_sms) * 16;
         exp_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(X, outer, kdim,
                                                                            s_outer, exp_out);
-        const int64_t total = outer * (ld_res >> 3);
-        int64_t sblocks = (total + 255) / 256;
-        if (sblocks > cap) sblocks = cap;
+        const int64_t chunks = ld_res >> 3;
+        int64_t gx = (chunks + 255) / 256;
+        if (gx > cap) gx = cap;
+        int64_t gy = cap / gx;
+        if (gy > outer) gy = outer;
+        if (gy > 65535) gy = 65535;
+        if (gy < 1) gy = 1;
+        const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy));
         if (C.symmetric)
-            split_rows_kernel<true><<<static_cast<unsigned>(sblocks), 256, 0, stream>>>(
-                X, outer, kdim, s_outer, exp_out, res, ld_res, plane, C);
+            split_rows_kernel<true><<<grid, 256, 0, stream>>>(X, outer, kdim, s_outer, exp_out,
+                                                              res, ld_res, plane, C);
         else
-            split_rows_kernel<false><<<static_cast<unsigned>(sblocks), 256, 0, stream>>>(
-                X, outer, kdim, s_outer, exp_out, res, ld_res, plane, C);
+            split_rows_kernel<false><<<grid, 256, 0, stream>>>(X, outer, kdim, s_outer, exp_out,
+                                                               res, ld_res, plane, C);
     } else {
         const int64_t blocks = (outer + 31) / 32;
         exp_cols_kernel<<<static_cast<unsigned>(blocks), 1024, 0, stream>>>(X, outer, kdim, s_k,
