@@ -58,6 +58,11 @@ def parse_args():
     p.add_argument("--n-moduli", type=int, default=None,
                    help="fix the moduli count (precision lowered if too few)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--workload", choices=["gemm", "lu", "cholesky", "rsvd"], default="gemm",
+                   help="gemm: the CRT GEMM line (default); lu / cholesky / rsvd: the callers "
+                        "of the CRT GEMM timed end to end with their backward errors")
+    p.add_argument("--n", type=int, default=None, help="matrix order (lu, cholesky) or rows "
+                   "(rsvd); default 16384 / 16384 / 65536")
     return p.parse_args()
 
 
@@ -487,10 +492,70 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_factorization(args):
+    """LU / Cholesky / randomized SVD with every trailing-update or projection GEMM on the CRT
+    kernels, timed end to end on one GPU, with the backward error and torch's own float64
+    routine on the same matrix for context."""
+    import torch
+
+    import tensor_inv_b200 as ti
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def timed(fn):
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        out = fn()
+        torch.cuda.synchronize(dev)
+        return out, time.perf_counter() - t0
+
+    line = {"workload": args.workload, "data": "synthetic, seeded, generated on the device",
+            "device": torch.cuda.get_device_name(dev)}
+    if args.workload == "lu":
+        n = args.n or 16384
+        A = torch.randn(n, n, generator=g, dtype=torch.float64, device=dev)
+        (P, L, U), t = timed(lambda: ti.lu(A, block_size=256))
+        err = (torch.linalg.norm(P @ A - L @ U) / torch.linalg.norm(A)).item()
+        _, t_ref = timed(lambda: torch.linalg.lu_factor(A))
+        line.update({"n": n, "block": 256, "seconds": t, "backward_error_fro": err,
+                     "torch_lu_factor_seconds": t_ref,
+                     "trailing_update_tflop": sum(2.0 * (n - j) ** 2 * 256
+                                                  for j in range(256, n, 256)) / 1e12})
+    elif args.workload == "cholesky":
+        n = args.n or 16384
+        X = torch.randn(n, n, generator=g, dtype=torch.float64, device=dev)
+        A = X @ X.T / n + 1e-6 * torch.eye(n, dtype=torch.float64, device=dev)
+        del X
+        L, t = timed(lambda: ti.cholesky(A, block_size=256))
+        err = (torch.linalg.norm(A - L @ L.T) / torch.linalg.norm(A)).item()
+        _, t_ref = timed(lambda: torch.linalg.cholesky(A))
+        line.update({"n": n, "block": 256, "seconds": t, "backward_error_fro": err,
+                     "torch_cholesky_seconds": t_ref})
+    else:
+        m = args.n or 65536
+        n, r = 8192, 256
+        Uq, _ = torch.linalg.qr(torch.randn(m, r, generator=g, dtype=torch.float64, device=dev))
+        Vq, _ = torch.linalg.qr(torch.randn(n, r, generator=g, dtype=torch.float64, device=dev))
+        sig = 0.95 ** torch.arange(r, dtype=torch.float64, device=dev)
+        A = (Uq * sig) @ Vq.T + 1e-8 * torch.randn(m, n, generator=g, dtype=torch.float64,
+                                                    device=dev)
+        torch.manual_seed(1)
+        (U, S, Vt), t = timed(lambda: ti.rsvd(A, rank=r, n_oversamples=10, n_power_iter=2))
+        err = (torch.linalg.norm(A - (U * S) @ Vt) / torch.linalg.norm(A)).item()
+        sv_err = ((S - sig).abs().max() / sig[0]).item()
+        line.update({"m": m, "n": n, "rank": r, "oversampling": 10, "power_iterations": 2,
+                     "seconds": t, "relative_error_fro": err, "max_singular_value_error": sv_err})
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload != "gemm":
+        run_factorization(args)
     else:
         run_ours(args)
 
