@@ -107,7 +107,7 @@ int ti_crt_reconstruct(const int32_t *residues, const int32_t *moduli, int n_mod
                        int64_t cols, double *out, int64_t ldo, void *stream);
 
 /* Moduli sets.  TI_MODULI_PRIMES is the reference's (the first N odd primes, 3..127,
-   N from _n_moduli).  TI_MODULI_WIDE is the opt-in extension of the survey's config 2:
+   N from _n_moduli).  TI_MODULI_WIDE is an opt-in extension:
    pairwise-coprime odd moduli up to 255 (255, 253, 251, 247, 241, 239, 233, 229, 227, 223,
    217, 211, 199, 197, 193, 191), at most 16.  With the automatic count, WIDE keeps every
    bit of the input precision, so its outputs are bit-identical to PRIMES with about a
@@ -122,7 +122,7 @@ typedef struct ti_crt_options {
                                fewest moduli that keep `bits`).  Otherwise exactly this many
                                (PRIMES <= 25, WIDE <= 16); when they cannot hold 2*k*2^(2*bits)
                                the precision is lowered to the largest b with
-                               prod(moduli) > 2*k*2^(2*b), the config-2 moduli sweep */
+                               prod(moduli) > 2*k*2^(2*b) (a moduli-count sweep) */
     void *stage_events[4];  /* optional cudaEvent_t, recorded before K1, before the first K2,
                                after the last K2 (before the last K3) and at the end; NULL
                                entries are skipped */
@@ -164,7 +164,7 @@ int ti_crt_matmul(const double *A, int64_t sa0, int64_t sa1, const double *B, in
 /*
  * ti_crt_matmul with options (moduli set, moduli count, profiling events).  With the
  * defaults it is ti_crt_matmul.  No counterpart in the reference, which has no options:
- * it extends crt_matmul.py:101 with the opt-in moduli set of the survey's config 2.
+ * it extends crt_matmul.py:101 with an opt-in moduli set and moduli count.
  */
 int ti_crt_matmul_ex(const double *A, int64_t sa0, int64_t sa1, const double *B, int64_t sb0,
                      int64_t sb1, double *C, int64_t ldc, int64_t m, int64_t n, int64_t k,

@@ -14,7 +14,7 @@ namespace ti {
 cudaError_t launch_split(const double *X, int64_t outer, int64_t kdim, int64_t s_outer,
                          int64_t s_k, const SplitConst &C, int32_t *exp_out, int8_t *res,
                          int64_t ld_res, int num_sms, cudaStream_t stream, int64_t plane = 0,
-                         int blocks_per_sm = 8);
+                         int blocks_per_sm = 8, int *err = nullptr);
 cudaError_t launch_residue_gemm(const int8_t *a_res, const int8_t *b_res, int64_t m, int64_t n,
                                 int64_t kdim, int64_t ld, int n_mod, const ModMagic &mm,
                                 void *out, int64_t ldo, int out_i32, int *err, int num_sms,
@@ -24,6 +24,14 @@ cudaError_t launch_crt(const void *R, bool in_u8, int64_t ldr, int64_t plane, in
                        int64_t cols, const int32_t *row_exp, const int32_t *col_exp, double *C,
                        int64_t ldc, int out_mode, const CrtConst &K, int num_sms,
                        cudaStream_t stream, int blocks_per_sm = 8);
+cudaError_t launch_split_tc(const double *X, int64_t outer, int64_t kdim, int64_t s_outer,
+                            int64_t s_k, const SplitConst &C, const int32_t *exps, int8_t *res,
+                            int64_t ld_res, int64_t plane, int *err, int num_sms,
+                            cudaStream_t stream);
+cudaError_t launch_crt_tc(const uint8_t *R, int64_t ldr, int64_t plane, int64_t rows,
+                          int64_t cols, const int32_t *row_exp, const int32_t *col_exp, double *C,
+                          int64_t ldc, int out_mode, const CrtConst &K, int *err, int num_sms,
+                          cudaStream_t stream);
 int64_t gemm_output_tiles(int64_t m, int64_t n);
 size_t fused_scratch_bytes(int n_mod, int num_ctas);
 cudaError_t launch_fused_gemm_crt(const int8_t *a_res, const int8_t *b_res, int64_t m, int64_t n,
@@ -47,6 +55,22 @@ static int path_override() {
 
 static bool use_fused(int64_t m, int64_t n) {
     return path_override() == 1 && gemm_output_tiles(m, n) >= 1;
+}
+
+// K3 on uint8 t-planes: the tensor-core kernel (ti_crt_tc.cu) by default; TI_CRT_K3=simt
+// selects the SIMT kernel (ti_crt.cu), which gives the same bits, for comparisons.  `sms`
+// caps the CTAs (a share of the SMs when the launch runs beside a GEMM).
+static cudaError_t launch_k3(const uint8_t *R, int64_t ldr, int64_t plane, int64_t rows,
+                             int64_t cols, const int32_t *rexp, const int32_t *cexp, double *C,
+                             int64_t ldc, int out_mode, const CrtConst &K, int *err, int sms,
+                             cudaStream_t s, int blocks_per_sm = 8) {
+    const char *e = getenv("TI_CRT_K3");
+    if (e && !strcmp(e, "simt"))
+        return launch_crt(R, true, ldr, plane, rows, cols, rexp, cexp, C, ldc, out_mode, K, sms,
+                          s, blocks_per_sm);
+    int ctas = sms * blocks_per_sm / 8;
+    if (ctas < 1) ctas = 1;
+    return launch_crt_tc(R, ldr, plane, rows, cols, rexp, cexp, C, ldc, out_mode, K, err, ctas, s);
 }
 
 // The device error word: kernels record a bounded wait that ran out here.
@@ -570,9 +594,9 @@ static int crt_matmul_banded(const double *A, int64_t sa0, int64_t sa1, const do
         const double *Ab = A + r0 * sa0;
         if (sa1 == 1)
             return launch_split(Ab, rows, k, sa0, 1, SC, rexp + r0, ares + r0 * L.ldk, L.ldk,
-                                d.num_sms, st, a_plane, bps);
+                                d.num_sms, st, a_plane, bps, d.err);
         return launch_split(Ab, rows, k, 1, sa1, SC, rexp + r0, ares + r0 * L.ldk, L.ldk,
-                            d.num_sms, st, a_plane, bps);
+                            d.num_sms, st, a_plane, bps, d.err);
     };
     record(ev, 0, s);
     if (cudaEventRecord(P.fork, s) != cudaSuccess) return TI_ERR_CUDA;
@@ -581,8 +605,8 @@ static int crt_matmul_banded(const double *A, int64_t sa0, int64_t sa1, const do
         return TI_ERR_CUDA;
     // hi: B and the first band of A, at full occupancy (nothing to overlap yet)
     cudaError_t e;
-    if (sb0 == 1) e = launch_split(B, n, k, sb1, 1, SC, cexp, bres, L.ldk, d.num_sms, P.hi);
-    else e = launch_split(B, n, k, 1, sb0, SC, cexp, bres, L.ldk, d.num_sms, P.hi);
+    if (sb0 == 1) e = launch_split(B, n, k, sb1, 1, SC, cexp, bres, L.ldk, d.num_sms, P.hi, 0, 8, d.err);
+    else e = launch_split(B, n, k, 1, sb0, SC, cexp, bres, L.ldk, d.num_sms, P.hi, 0, 8, d.err);
     if (e != cudaSuccess) return TI_ERR_CUDA;
     if (split_a(0, P.hi, 8) != cudaSuccess) return TI_ERR_CUDA;
     if (cudaEventRecord(P.split_done[0], P.hi) != cudaSuccess) return TI_ERR_CUDA;
@@ -608,9 +632,9 @@ static int crt_matmul_banded(const double *A, int64_t sa0, int64_t sa1, const do
         }
         if (cudaStreamWaitEvent(P.lo, P.gemm_done[b], 0) != cudaSuccess) return TI_ERR_CUDA;
         if (b == bands - 1) record(ev, 2, P.lo);
-        e = launch_crt(R + r0 * L.ldr, true, L.ldr, r_plane, rows, n, rexp + r0, cexp,
-                       C + r0 * ldc, ldc, out_mode, KC, d.num_sms, P.lo,
-                       b == bands - 1 ? 8 : kSideBlocksPerSm);
+        e = launch_k3(R + r0 * L.ldr, L.ldr, r_plane, rows, n, rexp + r0, cexp, C + r0 * ldc,
+                      ldc, out_mode, KC, d.err, d.num_sms, P.lo,
+                      b == bands - 1 ? 8 : kSideBlocksPerSm);
         if (e != cudaSuccess) return TI_ERR_CUDA;
     }
     if (cudaEventRecord(P.hi_done, P.hi) != cudaSuccess ||
@@ -692,11 +716,11 @@ int ti_crt_matmul_ex(const double *A, int64_t sa0, int64_t sa1, const double *B,
     // K1: A as m vectors along k (rows), B as n vectors along k (columns)
     cudaError_t e;
     record(ev, 0, s);
-    if (sa1 == 1) e = launch_split(A, m, k, sa0, 1, SC, rexp, ares, L.ldk, d.num_sms, s);
-    else e = launch_split(A, m, k, 1, sa1, SC, rexp, ares, L.ldk, d.num_sms, s);
+    if (sa1 == 1) e = launch_split(A, m, k, sa0, 1, SC, rexp, ares, L.ldk, d.num_sms, s, 0, 8, d.err);
+    else e = launch_split(A, m, k, 1, sa1, SC, rexp, ares, L.ldk, d.num_sms, s, 0, 8, d.err);
     if (e != cudaSuccess) return TI_ERR_CUDA;
-    if (sb0 == 1) e = launch_split(B, n, k, sb1, 1, SC, cexp, bres, L.ldk, d.num_sms, s);
-    else e = launch_split(B, n, k, 1, sb0, SC, cexp, bres, L.ldk, d.num_sms, s);
+    if (sb0 == 1) e = launch_split(B, n, k, sb1, 1, SC, cexp, bres, L.ldk, d.num_sms, s, 0, 8, d.err);
+    else e = launch_split(B, n, k, 1, sb0, SC, cexp, bres, L.ldk, d.num_sms, s, 0, 8, d.err);
     if (e != cudaSuccess) return TI_ERR_CUDA;
     record(ev, 1, s);
     if (use_fused(m, n)) {
@@ -717,7 +741,7 @@ int ti_crt_matmul_ex(const double *A, int64_t sa0, int64_t sa1, const double *B,
     if (e != cudaSuccess) return e == cudaErrorInvalidValue ? TI_ERR_NO_DEVICE : TI_ERR_CUDA;
     // K3: exact CRT + inverse scaling
     record(ev, 2, s);
-    e = launch_crt(R, true, L.ldr, m * L.ldr, m, n, rexp, cexp, C, ldc, out_mode, KC, d.num_sms, s);
+    e = launch_k3(R, L.ldr, m * L.ldr, m, n, rexp, cexp, C, ldc, out_mode, KC, d.err, d.num_sms, s);
     record(ev, 3, s);
     return cuda_status(e);
 }
@@ -740,18 +764,18 @@ static int crt_band_compute(const double *A, int64_t sa0, int64_t sa1, const dou
     uint8_t *R = ws + L.off_r;
     cudaError_t e;
     if (split_b) {
-        if (sb0 == 1) e = launch_split(B, n, k, sb1, 1, SC, cexp, bres, L.ldk, d.num_sms, s);
-        else e = launch_split(B, n, k, 1, sb0, SC, cexp, bres, L.ldk, d.num_sms, s);
+        if (sb0 == 1) e = launch_split(B, n, k, sb1, 1, SC, cexp, bres, L.ldk, d.num_sms, s, 0, 8, d.err);
+        else e = launch_split(B, n, k, 1, sb0, SC, cexp, bres, L.ldk, d.num_sms, s, 0, 8, d.err);
         if (e != cudaSuccess) return TI_ERR_CUDA;
     }
-    if (sa1 == 1) e = launch_split(A, rows, k, sa0, 1, SC, rexp, ares, L.ldk, d.num_sms, s);
-    else e = launch_split(A, rows, k, 1, sa1, SC, rexp, ares, L.ldk, d.num_sms, s);
+    if (sa1 == 1) e = launch_split(A, rows, k, sa0, 1, SC, rexp, ares, L.ldk, d.num_sms, s, 0, 8, d.err);
+    else e = launch_split(A, rows, k, 1, sa1, SC, rexp, ares, L.ldk, d.num_sms, s, 0, 8, d.err);
     if (e != cudaSuccess) return TI_ERR_CUDA;
     e = launch_residue_gemm(ares, bres, rows, n, k, L.ldk, L.n_mod, SC.mm, R, L.ldr, 0, d.err,
                             d.num_sms, s, 0, 0, 0, KC.u);
     if (e != cudaSuccess) return e == cudaErrorInvalidValue ? TI_ERR_NO_DEVICE : TI_ERR_CUDA;
-    e = launch_crt(R, true, L.ldr, rows * L.ldr, rows, n, rexp, cexp, C, ldc, TI_OUT_STORE, KC,
-                   d.num_sms, s);
+    e = launch_k3(R, L.ldr, rows * L.ldr, rows, n, rexp, cexp, C, ldc, TI_OUT_STORE, KC, d.err,
+                  d.num_sms, s);
     return cuda_status(e);
 }
 // Device copies of A, B and C ahead of the ti_crt_matmul_ex workspace, 256-byte aligned.

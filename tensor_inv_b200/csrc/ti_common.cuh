@@ -130,6 +130,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait that lets the hardware suspend the thread for up to `hint_ns` while the phase is
+// incomplete (it resumes as soon as the phase completes), so long waits cost few issue slots.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity,
+                                                   uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Waits for the phase of `bar` with the given parity to complete.  Returns false when the
 // wait exceeds kWaitTimeoutNs or when another role of the CTA raised *abort.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
@@ -138,7 +153,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
     if (mbar_try_wait(a, parity)) return true;
     const unsigned long long t0 = globaltimer_ns();
     while (true) {
-        if (mbar_try_wait(a, parity)) return true;
+        if (mbar_try_wait_hint(a, parity, 20000u)) return true;
         if (*abort) return false;
         if (globaltimer_ns() - t0 > kWaitTimeoutNs) return false;
     }
@@ -235,11 +250,88 @@ __device__ __forceinline__ uint64_t make_sw128_kmajor_desc(uint32_t saddr) {
            (static_cast<uint64_t>(2) << 61);
 }
 
+// Shared-memory matrix descriptor for an MN-major 8-bit operand tile stored with the
+// 128-byte swizzle: each 128-byte row holds 128 consecutive M (or N) elements of one k,
+// rows of consecutive k at 128-byte stride form 1024-byte atoms of 8 k, atoms stacked at
+// 1024-byte stride (SBO).  The tile is exactly one atom wide along M, so the leading
+// offset (the stride between atoms along M) is never used; it is set to `lbo_bytes`.
+__device__ __forceinline__ uint64_t make_sw128_mnmajor_desc(uint32_t saddr, uint32_t lbo_bytes) {
+    return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) |
+           (static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16) |
+           (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
+           (static_cast<uint64_t>(2) << 61);
+}
+
+// Shared-memory matrix descriptor for a K-major 8-bit operand tile without swizzle: core
+// matrices of 8 rows x 16 bytes (128 contiguous bytes), `lbo` bytes apart along K and
+// `sbo` bytes apart along M (or N).  Layout type 0 (SWIZZLE_NONE), descriptor version 1.
+__device__ __forceinline__ uint64_t make_noswizzle_kmajor_desc(uint32_t saddr, uint32_t lbo,
+                                                               uint32_t sbo) {
+    return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) |
+           (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
+           (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (static_cast<uint64_t>(1) << 46);
+}
+
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy reads
+// (tensor-core operand fetches) of the same bytes.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Instruction descriptor of tcgen05.mma.kind::i8: D s32, A and B signed 8-bit, both
 // K-major, M x N tile.
 __host__ __device__ constexpr uint32_t make_idesc_i8(int M, int N) {
     return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
            (static_cast<uint32_t>(M >> 4) << 24);
 }
+
+// Instruction descriptor of tcgen05.mma.kind::i8 with unsigned 8-bit A stored MN-major and
+// unsigned 8-bit B stored K-major, D s32, M x N tile.
+__host__ __device__ constexpr uint32_t make_idesc_u8_amn(int M, int N) {
+    return (2u << 4) | (1u << 15) | (static_cast<uint32_t>(N >> 3) << 17) |
+           (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// Work units (a, b), b fastest with nb values, strided over a persistent grid
+// (unit u = a * nb + b takes u = blockIdx.x, blockIdx.x + gridDim.x, ...), advanced without
+// integer division.
+struct GridIter {
+    int64_t a, b, step_a, step_b, nb;
+    __device__ explicit GridIter(int64_t n_b)
+        : a(blockIdx.x / n_b), b(blockIdx.x % n_b), step_a(gridDim.x / n_b),
+          step_b(gridDim.x % n_b), nb(n_b) {}
+    __device__ __forceinline__ void next() {
+        a += step_a;
+        b += step_b;
+        if (b >= nb) {
+            b -= nb;
+            ++a;
+        }
+    }
+};
+
+// Instruction descriptor of tcgen05.mma.kind::i8 with unsigned 8-bit A and B, both K-major,
+// D s32, M x N tile.
+__host__ __device__ constexpr uint32_t make_idesc_u8(int M, int N) {
+    return (2u << 4) | (static_cast<uint32_t>(N >> 3) << 17) |
+           (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// 2-D tiled TMA load global -> shared, completing on `bar` (no multicast).
+__device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *map,
+                                            uint64_t *bar, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+// cuTensorMapEncodeTiled from the driver, looked up once (null if unavailable).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn get_encode_fn();
 
 }  // namespace ti

@@ -12,45 +12,12 @@
 // and outer contiguous (s_outer == 1, "cols", a transposed view), the latter through a
 // shared-memory transpose.  Both write 8 consecutive residues per thread and modulus
 // as one 8-byte store, so a warp writes whole 32-byte sectors.
-#include "ti_common.cuh"
+#include <cstdlib>
+#include <cstring>
+
+#include "ti_scale.cuh"
 
 namespace ti {
-
-__device__ __forceinline__ uint64_t abs_bits(double x) {
-    return static_cast<uint64_t>(__double_as_longlong(x)) & 0x7FFFFFFFFFFFFFFFull;
-}
-
-// frexp exponent of max(m, 1e-300) from the bit pattern of m = max |x| (non-negative).
-__device__ __forceinline__ int exp_from_maxbits(uint64_t mb) {
-    if (mb >= 0x7FF0000000000000ull) return kNonfiniteExp;  // inf or NaN in the vector
-    if (mb < 0x0010000000000000ull) return -996;             // zero or subnormal: clamp
-    int e = static_cast<int>(mb >> 52) - 1022;               // frexp exponent
-    return e < -996 ? -996 : e;                               // clamp(min=1e-300)
-}
-
-// round_half_even(|x| * 2^(bits - e)) for |x| < 2^e; also returns the sign of x.
-__device__ __forceinline__ uint64_t scaled_magnitude(double x, int bits, int e, bool &neg) {
-    const uint64_t u = static_cast<uint64_t>(__double_as_longlong(x));
-    neg = (u >> 63) != 0;
-    const int be = static_cast<int>((u >> 52) & 0x7FF);
-    const uint64_t f = u & 0x000FFFFFFFFFFFFFull;
-    uint64_t sig;
-    int ex;  // |x| = sig * 2^ex
-    if (be == 0) {
-        sig = f;
-        ex = -1074;
-    } else {
-        sig = f | 0x0010000000000000ull;
-        ex = be - 1075;
-    }
-    int sh = e - bits - ex;  // right shift, >= 0 because |x| < 2^e
-    if (sh <= 0) return sig << (-sh);  // sh == 0 only (kept general)
-    if (sh > 63) sh = 63;              // sig < 2^53: shifts >= 54 all round to zero
-    const uint64_t q = sig >> sh;
-    const uint64_t rem = sig & ((1ull << sh) - 1);
-    const uint64_t half = 1ull << (sh - 1);
-    return q + ((rem > half) || (rem == half && (q & 1)));
-}
 
 // Residue bytes of 8 signed values (magnitudes mag[j] < 2^53, signs neg[j]) mod p_i,
 // packed little-endian into two 32-bit words: floor-mod residues in [0, p).
@@ -277,22 +244,47 @@ __global__ void __launch_bounds__(256) split_cols_kernel(
 // ---------------------------------------------------------------------------------------
 // host launchers
 // ---------------------------------------------------------------------------------------
+cudaError_t launch_split_tc(const double *X, int64_t outer, int64_t kdim, int64_t s_outer,
+                            int64_t s_k, const SplitConst &C, const int32_t *exps, int8_t *res,
+                            int64_t ld_res, int64_t plane, int *err, int num_sms,
+                            cudaStream_t stream);
+
+// Symmetric residues go to the tensor-core kernel (ti_split_tc.cu) when `err` (the device
+// error word its bounded waits report to) is given and the layout suits its copies;
+// TI_SPLIT=simt keeps them on the SIMT kernels below, which give the same bytes, and
+// TI_SPLIT=tc reports an unsuitable layout as an error instead of falling back (tests).
+static int split_mode() {  // 0 simt, 1 tensor cores with fallback, 2 tensor cores only
+    const char *e = getenv("TI_SPLIT");
+    if (e && !strcmp(e, "simt")) return 0;
+    if (e && !strcmp(e, "tc")) return 2;
+    return 1;
+}
+
 // plane: bytes between the residue planes of consecutive moduli (0: outer * ld_res, the
 // operand's own planes; a row band of a larger operand passes the full operand's stride).
 // blocks_per_sm caps the grid so the kernel can share SMs with a concurrent GEMM.
 cudaError_t launch_split(const double *X, int64_t outer, int64_t kdim, int64_t s_outer,
                          int64_t s_k, const SplitConst &C, int32_t *exp_out, int8_t *res,
                          int64_t ld_res, int num_sms, cudaStream_t stream, int64_t plane,
-                         int blocks_per_sm) {
+                         int blocks_per_sm, int *err) {
     if (outer == 0) return cudaSuccess;
     if (plane == 0) plane = outer * ld_res;
     const int64_t cap = int64_t(num_sms) * blocks_per_sm;
+    const int mode = (C.symmetric && err) ? split_mode() : 0;
+    const bool try_tc = mode != 0;
+    int tc_ctas = static_cast<int>(cap / 8);
+    if (tc_ctas < 1) tc_ctas = 1;
     if (s_k == 1) {
         const int64_t warps_needed = outer;
         int64_t blocks = (warps_needed + 7) / 8;
         if (blocks > int64_t(num_sms) * 16) blocks = int64_t(num_sms) * 16;
         exp_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(X, outer, kdim,
                                                                            s_outer, exp_out);
+        if (try_tc) {
+            const cudaError_t e = launch_split_tc(X, outer, kdim, s_outer, 1, C, exp_out, res,
+                                                  ld_res, plane, err, tc_ctas, stream);
+            if (e != cudaErrorNotSupported || mode == 2) return e;
+        }
         const int64_t chunks = ld_res >> 3;
         int64_t gx = (chunks + 255) / 256;
         if (gx > cap) gx = cap;
@@ -311,6 +303,11 @@ cudaError_t launch_split(const double *X, int64_t outer, int64_t kdim, int64_t s
         const int64_t blocks = (outer + 31) / 32;
         exp_cols_kernel<<<static_cast<unsigned>(blocks), 1024, 0, stream>>>(X, outer, kdim, s_k,
                                                                             exp_out);
+        if (try_tc) {
+            const cudaError_t e = launch_split_tc(X, outer, kdim, 1, s_k, C, exp_out, res,
+                                                  ld_res, plane, err, tc_ctas, stream);
+            if (e != cudaErrorNotSupported || mode == 2) return e;
+        }
         const int64_t tiles = ((outer + kColTileO - 1) / kColTileO) *
                               ((ld_res + kColTileK - 1) / kColTileK);
         int64_t sblocks = tiles;

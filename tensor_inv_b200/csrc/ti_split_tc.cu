@@ -1,0 +1,465 @@
+// ti_split_tc.cu -- K1 with the residue arithmetic on the tensor cores.
+//
+// Same residues, bit for bit, as split_rows_kernel / split_cols_kernel with symmetric
+// residues (ti_split.cu); restates src/tensor_inv/crt_matmul.py:38-52 (_scale_to_int,
+// _residues) with the representative of each residue in [-(p-1)/2, (p-1)/2].
+//
+// Per element the scaled integer v = round_half_even(x * 2^(bits - e)), |v| <= 2^53, is
+// written as eight unsigned digits: b_0..b_6, the bytes of v mod 2^56, and b_7 = [v < 0], so
+//   v = sum_{j<7} b_j 2^(8j) - 2^56 b_7.
+// With c_(j,i) = 2^(8j) mod p_i (j < 7) and c_(7,i) = (-2^56) mod p_i, all in [0, p_i),
+//   T_i = sum_j b_j c_(j,i) == v (mod p_i),   0 <= T_i < 8 * 255 * 255 < 2^19,
+// an unsigned 8-bit matrix product with 32-bit accumulation.  G element groups share one
+// MMA through a block-diagonal weight matrix W[(g, i)][(g', j)] = [g == g'] c_(j,i)
+// (M = 128 rows = G groups x 128/G moduli slots, K = 8G bytes) times the digit matrix
+// B[(g', j)][n] = digit j of element (g', n) (N = 256).  D[(g, i)][n] = T_i of element (g, n)
+// lands in TMEM lane g * 128/G + i, so each epilogue thread owns one modulus of one group
+// and reduces consecutive elements of one vector:
+//   r = T - p * floor((T + h) / p)  in [-h, h],  h = (p - 1) / 2,
+// with the quotient umulhi(T + h, ceil(2^32 / p)), exact for T + h < 2^24.
+//
+// G = 8 (up to 16 moduli; K = 64, two MMAs of K = 32) or G = 4 (up to 32 moduli; K = 32).
+// A unit is G vectors x 256 consecutive k: G rows of a k-contiguous operand or G columns of
+// an outer-contiguous one, loaded by one 2-D TMA box of float64 (zero-filled past the
+// matrix).  Both operand tiles use the no-swizzle K-major layout: core matrices of 8 rows x
+// 16 bytes, 128 bytes apart along K, 8*K bytes apart along M/N.
+//
+// Roles (one CTA per SM, persistent over units; vector blocks outer, k blocks fastest):
+//   warp 0       TMA producer: float64 tiles, 4-stage ring.
+//   warp 1       TMEM allocator (512 columns) + MMA issuer, 2 accumulators of 256 columns.
+//   warps 2..5   digits: scale each element, split it into 8 digits, store the B operand
+//                (2-stage ring).
+//   warps 6..13  epilogue: warp w reads TMEM lane quadrant w % 4, column half (w - 6) / 4.
+// Every wait is bounded; on timeout the CTA raises an error word, drains its in-flight
+// copies and MMAs, frees TMEM and exits.
+#include <atomic>
+#include <cstring>
+
+#include "ti_scale.cuh"
+
+namespace ti {
+
+template <int kG>
+struct SplitTcCfg {
+    static constexpr int kSlots = 128 / kG;          // moduli slots per element group
+    static constexpr int kK = 8 * kG;                // digit bytes per B column (MMA K)
+    static constexpr int kN = 256;                   // elements per vector per unit (MMA N)
+    static constexpr int kXStages = 4;
+    static constexpr int kXBytes = kG * kN * 8;      // float64 tile
+    static constexpr int kBStages = 2;
+    static constexpr int kBBytes = kN * kK;          // digit tile
+    static constexpr int kWBytes = 128 * kK;         // weights
+    static constexpr uint32_t kSbo = kK * 8;         // stride of 8-row groups
+    static constexpr int kPairs = kG;                // element pairs per digit thread per unit
+    static constexpr size_t kUsed =
+        size_t(kXStages) * kXBytes + size_t(kBStages) * kBBytes + kWBytes + 1024 + 256;
+    // at least 120 KB, so a second CTA (of this kernel, which takes all 512 TMEM columns)
+    // never lands on the same SM and waits for TMEM
+    static constexpr size_t kSmem = kUsed > 120 * 1024 ? kUsed : 120 * 1024;
+};
+
+constexpr int kSpDigitThreads = 128, kSpEpiThreads = 256;
+constexpr int kSpThreads = 64 + kSpDigitThreads + kSpEpiThreads;  // 448
+constexpr uint32_t kSpTmemCols = 512;
+constexpr uint32_t kSpIdesc = make_idesc_u8(128, 256);
+
+struct SplitTcParams {
+    int64_t outer, kdim, ld_res, plane;
+    int64_t vec_blocks, k_blocks;
+    const int32_t *exps;
+    int8_t *res;
+    int bits, n_mod;
+    int *err;
+    uint32_t p[kMaxModuli];
+};
+
+__device__ __forceinline__ void sp_raise(const SplitTcParams &P, volatile int *abort, int code) {
+    *abort = 1;
+    atomicCAS(P.err, 0, code);
+}
+
+__device__ __forceinline__ void sp_drain_wait(const SplitTcParams &P, uint64_t *bar,
+                                              uint32_t parity) {
+    const uint32_t a = smem_u32(bar);
+    const unsigned long long t0 = globaltimer_ns();
+    while (!mbar_try_wait(a, parity)) {
+        if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+            atomicCAS(P.err, 0, kErrTimeoutDrain);
+            return;
+        }
+    }
+}
+
+// 2^k as a float64, -1022 <= k <= 1023.
+__device__ __forceinline__ double pow2_normal(int k) {
+    return __longlong_as_double(static_cast<long long>(k + 1023) << 52);
+}
+
+// The eight digits of the scaled element as one little-endian word (0 for a vector with a
+// non-finite entry, whose residues are all zero).
+// v = round_half_even(x * 2^n), n = bits - e, in float64 arithmetic: |x| < 2^e, so
+// |x * 2^n| < 2^bits <= 2^53 and -1016 <= n <= 1049.  For n >= 0 the two power-of-two
+// factors (2^min(n,1023), then the rest) only scale up, so both products are exact (no
+// overflow; a subnormal x scales exactly).  For n < 0 the single product is exact unless it
+// is below 2^-1022, and then both it and the exact value round to 0.  The conversion rounds
+// to nearest-even, so v equals the integer-arithmetic result of scaled_magnitude.
+__device__ __forceinline__ uint64_t digits8(double x, int bits, int e) {
+    if (e == kNonfiniteExp) return 0;
+    const int n = bits - e;
+    const int n1 = n < 1023 ? n : 1023;
+    const double y = (x * pow2_normal(n1)) * pow2_normal(n - n1);
+    const long long v = __double2ll_rn(y);
+    return (static_cast<uint64_t>(v) & 0x00FFFFFFFFFFFFFFull) | (v < 0 ? (1ull << 56) : 0ull);
+}
+
+template <int kG, bool kRows>
+__global__ void __launch_bounds__(kSpThreads, 1)
+    split_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ SplitTcParams P) {
+    using Cfg = SplitTcCfg<kG>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // operand tiles first (weights, digits), then the float64 ring and the barriers
+    uint8_t *sW = smem;
+    uint8_t *sB = sW + Cfg::kWBytes;
+    uint8_t *sX = sB + Cfg::kBStages * Cfg::kBBytes;
+    uint64_t *xfull = reinterpret_cast<uint64_t *>(sX + Cfg::kXStages * Cfg::kXBytes);
+    uint64_t *xempty = xfull + Cfg::kXStages;
+    uint64_t *bfull = xempty + Cfg::kXStages;
+    uint64_t *bempty = bfull + Cfg::kBStages;
+    uint64_t *tfull = bempty + Cfg::kBStages;  // [2]
+    uint64_t *tempty = tfull + 2;              // [2]
+    uint64_t *drain = tempty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    // weights: row m = g * kSlots + i, column k = g * 8 + j (zero outside the diagonal blocks
+    // and for slots i >= n_mod)
+    for (int i = threadIdx.x; i < Cfg::kWBytes / 16; i += blockDim.x)
+        reinterpret_cast<uint4 *>(sW)[i] = make_uint4(0u, 0u, 0u, 0u);
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < 128 * 8; idx += blockDim.x) {
+        const int m = idx >> 3, j = idx & 7;
+        const int g = m / Cfg::kSlots, i = m - g * Cfg::kSlots;
+        if (i >= P.n_mod) continue;
+        const uint32_t p = P.p[i];
+        uint32_t t = 1;
+        for (int s = 0; s < (j < 7 ? j : 7); ++s) t = (t * 256u) % p;  // 2^(8 min(j,7)) mod p
+        const uint32_t c = j < 7 ? t : (t == 0 ? 0u : p - t);          // j = 7: (-2^56) mod p
+        const int k = g * 8 + j;
+        sW[(m >> 3) * Cfg::kSbo + (k >> 4) * 128 + (m & 7) * 16 + (k & 15)] =
+            static_cast<uint8_t>(c);
+    }
+    fence_proxy_async_smem();
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < Cfg::kXStages; ++s) {
+            mbar_init(&xfull[s], 1);
+            mbar_init(&xempty[s], kSpDigitThreads);
+        }
+        for (int s = 0; s < Cfg::kBStages; ++s) {
+            mbar_init(&bfull[s], kSpDigitThreads);
+            mbar_init(&bempty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], kSpEpiThreads);
+        }
+        mbar_init(drain, 1);
+        *abort = 0;
+        fence_barrier_init();
+        prefetch_tensormap(&tmX);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, kSpTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer ----------------
+            int stage = 0;
+            uint32_t phase = 0, issued_mask = 0, issued_phase = 0;
+            bool ok = true;
+            for (GridIter it(P.k_blocks); it.a < P.vec_blocks; it.next()) {
+                const int64_t o0 = it.a * kG, l0 = it.b * Cfg::kN;
+                if (!mbar_wait(&xempty[stage], phase ^ 1, abort)) {
+                    sp_raise(P, abort, kErrTimeoutProducer);
+                    ok = false;
+                    break;
+                }
+                if (l0 < P.kdim) {
+                    mbar_arrive_expect_tx(&xfull[stage], Cfg::kXBytes);
+                    if (kRows)
+                        tma_load_2d(sX + stage * Cfg::kXBytes, &tmX, &xfull[stage],
+                                    static_cast<int>(l0), static_cast<int>(o0));
+                    else
+                        tma_load_2d(sX + stage * Cfg::kXBytes, &tmX, &xfull[stage],
+                                    static_cast<int>(o0), static_cast<int>(l0));
+                    issued_mask |= 1u << stage;
+                    issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+                } else {
+                    mbar_arrive(&xfull[stage]);  // padding columns only: no copy, zero digits
+                }
+                if (++stage == Cfg::kXStages) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+            if (!ok)
+                for (int s = 0; s < Cfg::kXStages; ++s)
+                    if ((issued_mask >> s) & 1) sp_drain_wait(P, &xfull[s], (issued_phase >> s) & 1);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            const uint32_t w_addr = smem_u32(sW);
+            int bs = 0;
+            uint32_t bph = 0;
+            bool ok = true, any_issued = false;
+            int64_t local = 0;
+            for (GridIter it(P.k_blocks); it.a < P.vec_blocks; it.next(), ++local) {
+                const int acc = static_cast<int>(local & 1);
+                const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort) ||
+                    !mbar_wait(&bfull[bs], bph, abort)) {
+                    sp_raise(P, abort, kErrTimeoutMma);
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t b_addr = smem_u32(sB + bs * Cfg::kBBytes);
+#pragma unroll
+                for (int kk = 0; kk < Cfg::kK / 32; ++kk)  // K = 32 bytes = 2 core matrices
+                    umma_i8(tmem_base + static_cast<uint32_t>(acc) * 256u,
+                            make_noswizzle_kmajor_desc(w_addr + kk * 256, 128, Cfg::kSbo),
+                            make_noswizzle_kmajor_desc(b_addr + kk * 256, 128, Cfg::kSbo),
+                            kSpIdesc, kk > 0 ? 1u : 0u);
+                any_issued = true;
+                umma_commit(&bempty[bs]);
+                umma_commit(&tfull[acc]);
+                if (++bs == Cfg::kBStages) {
+                    bs = 0;
+                    bph ^= 1;
+                }
+            }
+            if (!ok && any_issued) {
+                umma_commit(drain);
+                sp_drain_wait(P, drain, 0);
+            }
+        }
+    } else if (warp < 6) {
+        // ---------------- digits (warps 2..5) ----------------
+        const int dt = threadIdx.x - 64;
+        int xs = 0, bs = 0;
+        uint32_t xph = 0, bph = 0;
+        for (GridIter it(P.k_blocks); it.a < P.vec_blocks; it.next()) {
+            const int64_t o0 = it.a * kG, l0 = it.b * Cfg::kN;
+            if (!mbar_wait(&xfull[xs], xph, abort) || !mbar_wait(&bempty[bs], bph ^ 1, abort)) {
+                sp_raise(P, abort, kErrTimeoutEpilogue);
+                break;
+            }
+            const double *X = reinterpret_cast<const double *>(sX + xs * Cfg::kXBytes);
+            uint8_t *Bt = sB + bs * Cfg::kBBytes;
+            const bool live = l0 < P.kdim;
+            // exponents of the groups this thread touches: all kG (rows: a = j / 2) or the
+            // pair 2a, 2a+1 with a = dt % (kG/2) fixed (columns)
+            int ex[kG];
+#pragma unroll
+            for (int g = 0; g < kG; ++g) {
+                const bool mine = kRows || (g >> 1) == dt % (kG / 2);
+                ex[g] = (mine && o0 + g < P.outer) ? __ldg(P.exps + o0 + g) : kNonfiniteExp;
+            }
+#pragma unroll
+            for (int j = 0; j < Cfg::kPairs; ++j) {
+                // element pair (groups 2a and 2a+1, column n): 16 bytes of one B row
+                const int pi = dt + kSpDigitThreads * j;
+                const int a = kRows ? (pi >> 8) : (pi % (kG / 2));
+                const int n = kRows ? (pi & 255) : (pi / (kG / 2));
+                uint64_t d0 = 0, d1 = 0;
+                if (live) {
+                    double x0, x1;
+                    if (kRows) {
+                        x0 = X[(2 * a) * Cfg::kN + n];
+                        x1 = X[(2 * a + 1) * Cfg::kN + n];
+                    } else {
+                        const double2 v = *reinterpret_cast<const double2 *>(X + n * kG + 2 * a);
+                        x0 = v.x;
+                        x1 = v.y;
+                    }
+                    int e0, e1;
+                    if (kRows) {  // a is a compile-time function of j
+                        e0 = ex[2 * (j >> 1)];
+                        e1 = ex[2 * (j >> 1) + 1];
+                    } else {      // a = dt % (kG/2) for every j
+                        e0 = kNonfiniteExp;
+                        e1 = kNonfiniteExp;
+#pragma unroll
+                        for (int g = 0; g < kG; g += 2)
+                            if ((g >> 1) == a) {
+                                e0 = ex[g];
+                                e1 = ex[g + 1];
+                            }
+                    }
+                    d0 = digits8(x0, P.bits, e0);
+                    d1 = digits8(x1, P.bits, e1);
+                }
+                *reinterpret_cast<uint4 *>(Bt + (n >> 3) * Cfg::kSbo + a * 128 + (n & 7) * 16) =
+                    make_uint4(static_cast<uint32_t>(d0), static_cast<uint32_t>(d0 >> 32),
+                               static_cast<uint32_t>(d1), static_cast<uint32_t>(d1 >> 32));
+            }
+            fence_proxy_async_smem();  // digit stores before the tensor core reads them
+            mbar_arrive(&xempty[xs]);
+            mbar_arrive(&bfull[bs]);
+            if (++xs == Cfg::kXStages) {
+                xs = 0;
+                xph ^= 1;
+            }
+            if (++bs == Cfg::kBStages) {
+                bs = 0;
+                bph ^= 1;
+            }
+        }
+    } else {
+        // ---------------- epilogue (warps 6..13) ----------------
+        const int q = warp & 3;              // TMEM lane quadrant this warp may access
+        const int half = (warp - 6) >> 2;    // column half of the unit
+        const int L = q * 32 + lane;         // TMEM lane = weight row
+        const int g = L / Cfg::kSlots, i = L - g * Cfg::kSlots;
+        const bool mod_ok = i < P.n_mod;
+        const uint32_t p = mod_ok ? P.p[i] : 3u, h = p >> 1;
+        const uint32_t magic = static_cast<uint32_t>(((uint64_t(1) << 32) + p - 1) / p);
+        int64_t local = 0;
+        for (GridIter it(P.k_blocks); it.a < P.vec_blocks; it.next(), ++local) {
+            const int acc = static_cast<int>(local & 1);
+            const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+            if (!mbar_wait(&tfull[acc], acc_phase, abort)) {
+                sp_raise(P, abort, kErrTimeoutEpilogue);
+                break;
+            }
+            tc_fence_after();
+            const int64_t o = it.a * kG + g;
+            const int64_t l0 = it.b * Cfg::kN + half * 128;
+            const bool active = mod_ok && o < P.outer;
+            int8_t *dst = P.res + (active ? int64_t(i) * P.plane + o * P.ld_res + l0 : 0);
+            const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                                   static_cast<uint32_t>(acc) * 256u + half * 128;
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(tbase + c * 32, v);
+                tmem_wait_ld();
+                if (c == 3) {  // the accumulator is fully read
+                    tc_fence_before();
+                    mbar_arrive(&tempty[acc]);
+                }
+                const int64_t lc = l0 + c * 32;
+                if (!active || lc >= P.ld_res) continue;
+                uint32_t pk[8];
+#pragma unroll
+                for (int w = 0; w < 8; ++w) {
+                    uint32_t r[4];
+#pragma unroll
+                    for (int b = 0; b < 4; ++b) {
+                        const uint32_t T = v[4 * w + b];
+                        r[b] = T - __umulhi(T + h, magic) * p;  // low byte: the residue
+                    }
+                    pk[w] = __byte_perm(__byte_perm(r[0], r[1], 0x0040),
+                                        __byte_perm(r[2], r[3], 0x0040), 0x5410);
+                }
+                *reinterpret_cast<uint4 *>(dst + c * 32) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                if (lc + 16 < P.ld_res)
+                    *reinterpret_cast<uint4 *>(dst + c * 32 + 16) =
+                        make_uint4(pk[4], pk[5], pk[6], pk[7]);
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kSpTmemCols);
+    }
+}
+
+template <int kG, bool kRows>
+static cudaError_t launch_split_tc_t(const CUtensorMap &tm, const SplitTcParams &P, int num_sms,
+                                     cudaStream_t stream) {
+    static std::atomic<int> configured{-1};  // last device configured
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (configured.load() != dev) {
+        const cudaError_t e = cudaFuncSetAttribute(split_tc_kernel<kG, kRows>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   static_cast<int>(SplitTcCfg<kG>::kSmem));
+        if (e != cudaSuccess) return e;
+        configured.store(dev);
+    }
+    const int64_t units = P.vec_blocks * P.k_blocks;
+    const int64_t grid = units < num_sms ? units : num_sms;
+    split_tc_kernel<kG, kRows><<<static_cast<unsigned>(grid), kSpThreads, SplitTcCfg<kG>::kSmem,
+                                 stream>>>(tm, P);
+    return cudaGetLastError();
+}
+
+// Symmetric residues of one operand (exponents already in `exps`) on the tensor cores.
+// X is outer vectors of kdim elements, element (o, l) at X[o*s_outer + l*s_k], with either
+// s_k == 1 (rows) or s_outer == 1 (columns).  Writes res[i*plane + o*ld_res + l] for
+// l < ld_res (zero for l >= kdim).  Returns cudaErrorNotSupported when the layout does not
+// suit the 2-D copies (misaligned base or odd stride): the SIMT kernels cover that case.
+cudaError_t launch_split_tc(const double *X, int64_t outer, int64_t kdim, int64_t s_outer,
+                            int64_t s_k, const SplitConst &C, const int32_t *exps, int8_t *res,
+                            int64_t ld_res, int64_t plane, int *err, int num_sms,
+                            cudaStream_t stream) {
+    if (outer == 0) return cudaSuccess;
+    const bool rows = (s_k == 1);
+    const int64_t stride = rows ? s_outer : s_k;
+    if (!C.symmetric || C.n_mod > kMaxModuli || kdim < 1 ||
+        (reinterpret_cast<uintptr_t>(X) & 15) || (stride & 1) || stride < 2 ||
+        stride >= (int64_t(1) << 36) || (!rows && s_outer != 1) || (ld_res & 15) ||
+        (plane & 15) || (reinterpret_cast<uintptr_t>(res) & 15))
+        return cudaErrorNotSupported;
+    const EncodeTiledFn enc = get_encode_fn();
+    if (!enc) return cudaErrorNotSupported;
+    const int G = C.n_mod <= 16 ? 8 : 4;
+    CUtensorMap tm;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(rows ? kdim : outer),
+                                static_cast<cuuint64_t>(rows ? outer : kdim)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(stride) * 8};
+    const cuuint32_t box[2] = {rows ? 256u : static_cast<cuuint32_t>(G),
+                               rows ? static_cast<cuuint32_t>(G) : 256u};
+    const cuuint32_t estr[2] = {1, 1};
+    if (enc(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT64, 2, const_cast<double *>(X), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return cudaErrorNotSupported;
+    SplitTcParams P;
+    std::memset(&P, 0, sizeof(P));
+    P.outer = outer;
+    P.kdim = kdim;
+    P.ld_res = ld_res;
+    P.plane = plane;
+    P.vec_blocks = (outer + G - 1) / G;
+    P.k_blocks = (ld_res + 255) / 256;
+    P.exps = exps;
+    P.res = res;
+    P.bits = C.bits;
+    P.n_mod = C.n_mod;
+    P.err = err;
+    for (int i = 0; i < C.n_mod; ++i) P.p[i] = C.mm.p[i];
+    if (G == 8)
+        return rows ? launch_split_tc_t<8, true>(tm, P, num_sms, stream)
+                    : launch_split_tc_t<8, false>(tm, P, num_sms, stream);
+    return rows ? launch_split_tc_t<4, true>(tm, P, num_sms, stream)
+                : launch_split_tc_t<4, false>(tm, P, num_sms, stream);
+}
+
+}  // namespace ti

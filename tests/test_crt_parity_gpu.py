@@ -104,7 +104,7 @@ def _rand(shape, seed, phi=None, dtype=torch.float64):
 
 
 SHAPES = [
-    (1024, 1024, 1024, None),   # BASELINE config 1 shape, N(0,1)
+    (1024, 1024, 1024, None),   # 1024^3, N(0,1)
     (300, 500, 257, 2.0),
     (129, 257, 1, None),
     (133, 77, 1100, 1.0),
@@ -296,6 +296,106 @@ def test_fused_update_modes(ti, oracle, crt_path, alpha):
     _assert_bitexact(C, want)
 
 
+# ---------------------------------------------------------------------------------------
+# the two reconstruction kernels (tensor-core default, SIMT with TI_CRT_K3=simt)
+# ---------------------------------------------------------------------------------------
+@pytest.mark.parametrize("m,n,k,phi,moduli", [(1, 1, 1, None, None), (3, 129, 40, 2.0, None),
+                                              (130, 255, 300, 1.0, "wide"),
+                                              (517, 1000, 2049, 0.5, None),
+                                              (257, 384, 7200, 3.0, "wide")])
+def test_k3_kernels_agree(ti, oracle, monkeypatch, m, n, k, phi, moduli):
+    A = _rand((m, k), 6100 + m, phi).cuda()
+    B = _rand((k, n), 6200 + n, phi).cuda()
+    monkeypatch.setenv("TI_CRT_K3", "simt")
+    C_simt = ti.crt_matmul(A, B, moduli=moduli)
+    monkeypatch.delenv("TI_CRT_K3")
+    C_tc = ti.crt_matmul(A, B, moduli=moduli)
+    _assert_bitexact(C_tc, C_simt.cpu().numpy())
+    r1, c1 = min(m, 96), min(n, 160)
+    want = oracle.crt_matmul(A[:r1].cpu().numpy(), B[:, :c1].cpu().numpy(), 53)
+    _assert_bitexact(C_tc[:r1, :c1], want)
+
+
+# ---------------------------------------------------------------------------------------
+# the two split kernels (tensor-core default, SIMT with TI_SPLIT=simt)
+# ---------------------------------------------------------------------------------------
+def _view(X, layout):
+    """The same matrix as a row-major tensor ("c"), a transposed view ("t"), or a view with
+    an odd row stride ("odd"), which the tensor-core split hands to the SIMT kernels."""
+    if layout == "c":
+        return X.contiguous()
+    if layout == "t":
+        return X.t().contiguous().t()
+    big = torch.empty((X.shape[0], X.shape[1] + 1), dtype=X.dtype, device=X.device)
+    big[:, : X.shape[1]] = X
+    return big[:, : X.shape[1]]
+
+
+def _tc_layout_ok(X, k_axis):
+    """Whether the tensor-core split takes this operand (an even stride between the float64
+    rows or columns it copies), as the library decides."""
+    so, sk = (X.stride(0), X.stride(1)) if k_axis == 1 else (X.stride(1), X.stride(0))
+    st = so if sk == 1 else sk
+    return st >= 2 and st % 2 == 0
+
+
+@pytest.mark.parametrize("m,n,k,phi,moduli,la,lb", [
+    (1, 1, 1, None, None, "c", "c"),          # unit strides: SIMT fallback
+    (9, 8, 300, 2.0, "wide", "c", "c"),       # ragged vector block, k not a multiple of 256
+    (130, 254, 514, 1.0, None, "t", "t"),     # 25 primes: 4 groups per MMA; transposed views
+    (258, 384, 1024, 3.0, "wide", "t", "c"),
+    (1001, 64, 2, 1.0, "wide", "c", "c"),     # k = 2: one k block holding padding
+    (64, 96, 777, 0.5, "wide", "odd", "c"),   # odd stride: SIMT fallback for A
+    (500, 520, 2048, 1.0, "wide", "c", "t"),
+])
+def test_split_kernels_agree(ti, oracle, monkeypatch, m, n, k, phi, moduli, la, lb):
+    A = _view(_rand((m, k), 6400 + m, phi).cuda(), la)
+    B = _view(_rand((k, n), 6500 + n, phi).cuda(), lb)
+    monkeypatch.setenv("TI_SPLIT", "simt")
+    C_simt = ti.crt_matmul(A, B, moduli=moduli)
+    # tensor cores only (an unsuitable layout is an error) when both operands suit them
+    strict = _tc_layout_ok(A, 1) and _tc_layout_ok(B, 0)
+    monkeypatch.setenv("TI_SPLIT", "tc" if strict else "auto")
+    C_tc = ti.crt_matmul(A, B, moduli=moduli)
+    _assert_bitexact(C_tc, C_simt.cpu().numpy())
+    r1, c1 = min(m, 64), min(n, 96)
+    want = oracle.crt_matmul(A[:r1].cpu().numpy(), B[:, :c1].cpu().numpy(), 53)
+    _assert_bitexact(C_tc[:r1, :c1], want)
+
+
+def test_split_tensor_core_nonfinite_and_extremes(ti, oracle, monkeypatch):
+    m, n, k = 40, 48, 600
+    A = _rand((m, k), 6601, 4.0)
+    B = _rand((k, n), 6602, 4.0)
+    A[3, 7] = float("nan")
+    B[5, 11] = float("-inf")
+    A[10] = 0.0                                  # zero row: exponent clamp
+    A[11, :5] = torch.tensor([5e-324, -5e-324, 2.2e-308, -1.7e308, 1.7e308], dtype=torch.float64)
+    B[:, 20] = -2.0 ** -1070                     # subnormal column
+    monkeypatch.setenv("TI_SPLIT", "simt")
+    C = ti.crt_matmul(A.cuda(), B.cuda(), moduli="wide").cpu()
+    assert torch.isnan(C[3]).all() and torch.isnan(C[:, 11]).all()
+    monkeypatch.setenv("TI_SPLIT", "tc")
+    _assert_bitexact(ti.crt_matmul(A.cuda(), B.cuda(), moduli="wide"), C.numpy())
+    keep_r = [i for i in range(m) if i != 3]
+    keep_c = [j for j in range(n) if j != 11]
+    want = oracle.crt_matmul(A[keep_r].numpy(), B[:, keep_c].numpy(), 53)
+    _assert_bitexact(C[keep_r][:, keep_c], want)
+
+
+@pytest.mark.parametrize("alpha", [-1, 1])
+def test_k3_tensor_core_update_modes(ti, oracle, alpha):
+    m, n, k = 301, 259, 129
+    A = _rand((m, k), 6301)
+    B = _rand((k, n), 6302)
+    C0 = _rand((m, n), 6303)
+    prod = oracle.crt_matmul(A.numpy(), B.numpy(), 53)
+    want = C0.numpy() - prod if alpha == -1 else C0.numpy() + prod
+    C = C0.cuda()
+    ti.crt_matmul_update(C, A.cuda(), B.cuda(), alpha=alpha)
+    _assert_bitexact(C, want)
+
+
 def test_fused_nonfinite(ti, oracle, crt_path):
     crt_path("fused")
     A = _rand((40, 60), 91)
@@ -311,7 +411,7 @@ def test_fused_nonfinite(ti, oracle, crt_path):
 
 
 # ---------------------------------------------------------------------------------------
-# opt-in wide moduli (pairwise-coprime odd moduli <= 255, the survey's config 2)
+# opt-in wide moduli (pairwise-coprime odd moduli <= 255)
 # ---------------------------------------------------------------------------------------
 @pytest.mark.parametrize("case", golden_cases())
 def test_wide_moduli_full_precision_is_bit_identical(ti, case):
@@ -335,7 +435,7 @@ def test_wide_moduli_vs_reference_scheme(ti, oracle, m, n, k, phi):
 @pytest.mark.parametrize("n_mod", [12, 13, 14, 15, 16])
 @pytest.mark.parametrize("moduli", ["wide", "primes"])
 def test_moduli_sweep_vs_oracle(ti, oracle, n_mod, moduli):
-    """Config-2 sweep: N moduli, precision lowered to what N moduli can hold; bit-exact
+    """Moduli-count sweep: N moduli, precision lowered to what N moduli can hold; bit-exact
     against the reference algorithm restated with the same moduli and precision."""
     from tensor_inv_b200 import _native
 
