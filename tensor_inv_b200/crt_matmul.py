@@ -135,7 +135,7 @@ def crt_matmul(A, B, *, moduli=None, n_moduli=None):
     ``moduli='wide'`` uses pairwise-coprime odd moduli up to 255 instead of the primes up
     to 127; with ``n_moduli=None`` it takes the fewest that keep every bit of the input
     precision, so the result is bit-identical with about a third fewer residue GEMMs.
-    ``n_moduli=N`` fixes the count (the survey's config-2 sweep); if N moduli cannot hold
+    ``n_moduli=N`` fixes the count (a moduli-count sweep); if N moduli cannot hold
     the full precision, the scaling keeps the largest b with prod(moduli) > 2*k*2^(2b) bits.
     """
     bits = _check_dtype(A)
