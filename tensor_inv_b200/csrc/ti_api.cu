@@ -19,7 +19,8 @@ cudaError_t launch_residue_gemm(const int8_t *a_res, const int8_t *b_res, int64_
                                 int64_t kdim, int64_t ld, int n_mod, const ModMagic &mm,
                                 void *out, int64_t ldo, int out_i32, int *err, int num_sms,
                                 cudaStream_t stream, int64_t a_plane = 0, int64_t b_plane = 0,
-                                int64_t out_plane = 0, const uint32_t *weights = nullptr);
+                                int64_t out_plane = 0, const uint32_t *weights = nullptr,
+                                bool unsigned_ops = false);
 cudaError_t launch_crt(const void *R, bool in_u8, int64_t ldr, int64_t plane, int64_t rows,
                        int64_t cols, const int32_t *row_exp, const int32_t *col_exp, double *C,
                        int64_t ldc, int out_mode, const CrtConst &K, int num_sms,
@@ -38,7 +39,7 @@ cudaError_t launch_fused_gemm_crt(const int8_t *a_res, const int8_t *b_res, int6
                                   int64_t kdim, int64_t ld, const CrtConst &K,
                                   const int32_t *row_exp, const int32_t *col_exp, double *C,
                                   int64_t ldc, int out_mode, uint8_t *scratch, int grid, int *err,
-                                  cudaStream_t stream);
+                                  cudaStream_t stream, bool unsigned_ops);
 
 // The fused GEMM+CRT kernel (K2+K3 in one launch) is opt-in (TI_CRT_PATH=fused): measured
 // on B200 at 8192^3 its tile-major order (all moduli of one tile back to back) costs the
@@ -215,10 +216,22 @@ static bool make_split_const(const int32_t *moduli, int n_mod, int bits, bool sy
         const uint64_t p = static_cast<uint32_t>(moduli[i]);
         C.w32[i] = static_cast<uint32_t>((uint64_t(1) << 32) % p);
         C.w16[i] = static_cast<uint32_t>((uint64_t(1) << 16) % p);
-        C.bigp[i] = static_cast<uint32_t>(p * (((uint64_t(1) << 29) + p - 1) / p));
+        C.bigp[i] = static_cast<uint32_t>(p * (((uint64_t(1) << 30) + p - 1) / p));
         C.offs[i] = static_cast<uint32_t>(p * ((uint64_t(549388288) + p - 1) / p));
     }
     return true;
+}
+
+// Residue representative on the matmul path.  Floor-mod residues in [0, p) (unsigned bytes,
+// an unsigned residue GEMM) when k * (p_max - 1)^2 leaves the int32 accumulator below
+// 2^31 - 256, which the epilogue's exact reduction needs; otherwise symmetric residues in
+// [-(p-1)/2, (p-1)/2] (signed bytes).  The products mod p, and so every output bit, are the
+// same for either representative; the unsigned form costs the split one operation less per
+// residue.
+static bool floor_mod_residues(const Plan &P, int64_t k) {
+    int64_t pmax = 0;
+    for (int i = 0; i < P.n_mod; ++i) pmax = P.moduli[i] > pmax ? P.moduli[i] : pmax;
+    return k * (pmax - 1) * (pmax - 1) <= (int64_t(1) << 31) - 256;
 }
 
 // Pairwise-coprime moduli with product below 2^127 (so every lifted value fits 128 bits).
@@ -622,7 +635,7 @@ static int crt_matmul_banded(const double *A, int64_t sa0, int64_t sa1, const do
             return TI_ERR_CUDA;
         e = launch_residue_gemm(ares + r0 * L.ldk, bres, rows, n, k, L.ldk, L.n_mod, SC.mm,
                                 R + r0 * L.ldr, L.ldr, 0, d.err, d.num_sms, P.hi, a_plane,
-                                b_plane, r_plane, KC.u);
+                                b_plane, r_plane, KC.u, !SC.symmetric);
         if (e != cudaSuccess) return e == cudaErrorInvalidValue ? TI_ERR_NO_DEVICE : TI_ERR_CUDA;
         if (cudaEventRecord(P.gemm_done[b], P.hi) != cudaSuccess) return TI_ERR_CUDA;
         // lo: split of the next band, then the reconstruction of this one
@@ -698,10 +711,10 @@ int ti_crt_matmul_ex(const double *A, int64_t sa0, int64_t sa1, const double *B,
     SplitConst SC;
     CrtConst KC;
     const Plan &PL = L.plan;
-    // symmetric residues on the matmul path for either moduli set: the residue products
-    // mod p do not depend on the representative (the stage entry ti_crt_split keeps the
-    // reference's floor-mod bytes)
-    if (!make_split_const(PL.moduli, PL.n_mod, PL.bits, true, SC)) return TI_ERR_UNSUPPORTED;
+    // the residue representative follows floor_mod_residues (the products mod p do not
+    // depend on it; the stage entry ti_crt_split keeps the reference's floor-mod bytes)
+    if (!make_split_const(PL.moduli, PL.n_mod, PL.bits, !floor_mod_residues(PL, k), SC))
+        return TI_ERR_UNSUPPORTED;
     if (!make_crt_const(PL.moduli, PL.n_mod, PL.bits, KC)) return TI_ERR_UNSUPPORTED;
 
     int bands = opt && opt->bands > 0 ? opt->bands : auto_bands(m);
@@ -729,7 +742,7 @@ int ti_crt_matmul_ex(const double *A, int64_t sa0, int64_t sa1, const double *B,
         if (grid > d.num_sms) grid = d.num_sms;
         if (grid > kFusedMaxCtas) grid = kFusedMaxCtas;
         e = launch_fused_gemm_crt(ares, bres, m, n, k, L.ldk, KC, rexp, cexp, C, ldc, out_mode, R,
-                                  static_cast<int>(grid), d.err, s);
+                                  static_cast<int>(grid), d.err, s, !SC.symmetric);
         record(ev, 2, s);
         record(ev, 3, s);
         if (e != cudaSuccess) return e == cudaErrorInvalidValue ? TI_ERR_NO_DEVICE : TI_ERR_CUDA;
@@ -737,7 +750,7 @@ int ti_crt_matmul_ex(const double *A, int64_t sa0, int64_t sa1, const double *B,
     }
     // K2: per-modulus residue GEMMs, mod-reduced to uint8 planes
     e = launch_residue_gemm(ares, bres, m, n, k, L.ldk, L.n_mod, SC.mm, R, L.ldr, 0, d.err,
-                            d.num_sms, s, 0, 0, 0, KC.u);
+                            d.num_sms, s, 0, 0, 0, KC.u, !SC.symmetric);
     if (e != cudaSuccess) return e == cudaErrorInvalidValue ? TI_ERR_NO_DEVICE : TI_ERR_CUDA;
     // K3: exact CRT + inverse scaling
     record(ev, 2, s);
@@ -772,7 +785,7 @@ static int crt_band_compute(const double *A, int64_t sa0, int64_t sa1, const dou
     else e = launch_split(A, rows, k, 1, sa1, SC, rexp, ares, L.ldk, d.num_sms, s, 0, 8, d.err);
     if (e != cudaSuccess) return TI_ERR_CUDA;
     e = launch_residue_gemm(ares, bres, rows, n, k, L.ldk, L.n_mod, SC.mm, R, L.ldr, 0, d.err,
-                            d.num_sms, s, 0, 0, 0, KC.u);
+                            d.num_sms, s, 0, 0, 0, KC.u, !SC.symmetric);
     if (e != cudaSuccess) return e == cudaErrorInvalidValue ? TI_ERR_NO_DEVICE : TI_ERR_CUDA;
     e = launch_k3(R, L.ldr, rows * L.ldr, rows, n, rexp, cexp, C, ldc, TI_OUT_STORE, KC, d.err,
                   d.num_sms, s);
@@ -840,7 +853,8 @@ int ti_crt_matmul_host(const double *A, int64_t sa0, int64_t sa1, const double *
     SplitConst SC;
     CrtConst KC;
     if (k > 0) {
-        if (!make_split_const(L.plan.moduli, L.plan.n_mod, L.plan.bits, true, SC) ||
+        if (!make_split_const(L.plan.moduli, L.plan.n_mod, L.plan.bits,
+                              !floor_mod_residues(L.plan, k), SC) ||
             !make_crt_const(L.plan.moduli, L.plan.n_mod, L.plan.bits, KC))
             return TI_ERR_UNSUPPORTED;
     }

@@ -61,7 +61,8 @@ struct SplitConst {
     ModMagic mm;
     uint32_t w32[kMaxModuli];   // 2^32 mod p
     uint32_t w16[kMaxModuli];   // 2^16 mod p
-    uint32_t bigp[kMaxModuli];  // p * ceil(2^29 / p): a multiple of p that is >= 2^29
+    uint32_t bigp[kMaxModuli];  // p * ceil(2^30 / p): a multiple of p above any piece sum
+                                // (a2*w32 + a1*w16 + a0 < 2^21*255 + 2^16*255 + 2^16 < 2^30)
     uint32_t offs[kMaxModuli];  // p * ceil(549388288 / p): a multiple of p above any |T|
                                 // (T = a2*w32 + a1*w16 + a0 of signed pieces, |T| < 549388288)
 };

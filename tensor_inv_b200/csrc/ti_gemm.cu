@@ -56,6 +56,7 @@ struct GemmParams {
     int64_t plane;     // elements between moduli planes
     int out_i32;       // 0: uint8 residues (|accumulator| <= 2^31 - 256); 1: int32, any int8
     int store_t;       // uint8 output holds t = (r * crt.u[i]) mod p instead of r
+    uint32_t idesc;    // MMA instruction descriptor: signed or unsigned 8-bit operands
     // fused output
     uint8_t *scratch;  // 2 slots x n_mod x 128 x 256 bytes per CTA
     const int32_t *row_exp, *col_exp;
@@ -287,7 +288,7 @@ __global__ void __launch_bounds__(gemm_threads(kFused), 1)
 #pragma unroll
                     for (int kk = 0; kk < kBK / 32; ++kk) {
                         // advance the start address by 32 bytes (2 x 16-byte units) per K step
-                        umma_i8(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, kIdesc,
+                        umma_i8(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, P.idesc,
                                 (kb | kk) != 0 ? 1u : 0u);
                     }
                     any_issued = true;
@@ -485,7 +486,7 @@ static cudaError_t configure(int dev) {
 static cudaError_t fill_common(GemmParams &P, CUtensorMap &tmA, CUtensorMap &tmB,
                                const int8_t *a_res, const int8_t *b_res, int64_t m, int64_t n,
                                int64_t kdim, int64_t ld, int n_mod, const ModMagic &mm, int *err,
-                               int64_t a_plane, int64_t b_plane) {
+                               int64_t a_plane, int64_t b_plane, bool unsigned_ops) {
     // kdim == 0 is handled by the callers; a map needs at least one column
     const int64_t kd = kdim > 0 ? kdim : 1;
     if (!make_plane_map(&tmA, a_res, kd, m, ld, n_mod, kBM, a_plane ? a_plane : ld * m))
@@ -502,6 +503,7 @@ static cudaError_t fill_common(GemmParams &P, CUtensorMap &tmA, CUtensorMap &tmB
     P.total_units = int64_t(P.tiles_m) * P.tiles_n * n_mod;
     P.mm = mm;
     P.err = err;
+    P.idesc = unsigned_ops ? make_idesc_u8(kBM, kBN) : kIdesc;
     return P.num_kb > 0 ? cudaSuccess : cudaErrorInvalidValue;
 }
 
@@ -515,11 +517,13 @@ int gemm_smem_bytes() { return static_cast<int>(kGemmSmemBytes); }
 // out_plane: elements between output planes (0: m * ldo).  Row bands of larger operands
 // pass their full operands' strides.
 // weights: if not null, the uint8 output holds t_i = (r_i * weights[i]) mod p_i.
+// unsigned_ops: the residue planes hold unsigned bytes (floor-mod residues up to 254)
+// instead of signed ones.
 cudaError_t launch_residue_gemm(const int8_t *a_res, const int8_t *b_res, int64_t m, int64_t n,
                                 int64_t kdim, int64_t ld, int n_mod, const ModMagic &mm,
                                 void *out, int64_t ldo, int out_i32, int *err, int num_sms,
                                 cudaStream_t stream, int64_t a_plane, int64_t b_plane,
-                                int64_t out_plane, const uint32_t *weights) {
+                                int64_t out_plane, const uint32_t *weights, bool unsigned_ops) {
     if (m == 0 || n == 0 || n_mod == 0) return cudaSuccess;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -527,7 +531,8 @@ cudaError_t launch_residue_gemm(const int8_t *a_res, const int8_t *b_res, int64_
     if (e != cudaSuccess) return e;
     CUtensorMap tmA, tmB;
     GemmParams P;
-    e = fill_common(P, tmA, tmB, a_res, b_res, m, n, kdim, ld, n_mod, mm, err, a_plane, b_plane);
+    e = fill_common(P, tmA, tmB, a_res, b_res, m, n, kdim, ld, n_mod, mm, err, a_plane, b_plane,
+                    unsigned_ops);
     if (e != cudaSuccess) return e;
     P.out = out;
     P.ldo = ldo;
@@ -559,7 +564,7 @@ cudaError_t launch_fused_gemm_crt(const int8_t *a_res, const int8_t *b_res, int6
                                   int64_t kdim, int64_t ld, const CrtConst &K,
                                   const int32_t *row_exp, const int32_t *col_exp, double *C,
                                   int64_t ldc, int out_mode, uint8_t *scratch, int grid, int *err,
-                                  cudaStream_t stream) {
+                                  cudaStream_t stream, bool unsigned_ops) {
     if (m == 0 || n == 0) return cudaSuccess;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -567,7 +572,8 @@ cudaError_t launch_fused_gemm_crt(const int8_t *a_res, const int8_t *b_res, int6
     if (e != cudaSuccess) return e;
     CUtensorMap tmA, tmB;
     GemmParams P;
-    e = fill_common(P, tmA, tmB, a_res, b_res, m, n, kdim, ld, K.n_mod, K.mm, err, 0, 0);
+    e = fill_common(P, tmA, tmB, a_res, b_res, m, n, kdim, ld, K.n_mod, K.mm, err, 0, 0,
+                    unsigned_ops);
     if (e != cudaSuccess) return e;
     P.scratch = scratch;
     P.row_exp = row_exp;

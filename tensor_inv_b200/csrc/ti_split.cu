@@ -29,9 +29,9 @@ __device__ __forceinline__ uint2 residues8(const uint32_t (&a2)[8], const uint32
     uint32_t out[2] = {0u, 0u};
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-        // mag = a2*2^32 + a1*2^16 + a0  ==>  t == mag (mod p), t < 2^29
+        // mag = a2*2^32 + a1*2^16 + a0  ==>  t == mag (mod p), t < 2^30
         uint32_t t = a2[j] * w32 + a1[j] * w16 + a0[j];
-        t = ((negmask >> j) & 1u) ? bigp - t : t;  // -mag (mod p), still < 2^30
+        t = ((negmask >> j) & 1u) ? bigp - t : t;  // -mag (mod p), bigp - t < 2^31
         const uint32_t r = mod_small(t, p, magic, shift);
         out[j >> 2] |= r << (8 * (j & 3));
     }
@@ -249,8 +249,8 @@ cudaError_t launch_split_tc(const double *X, int64_t outer, int64_t kdim, int64_
                             int64_t ld_res, int64_t plane, int *err, int num_sms,
                             cudaStream_t stream);
 
-// Symmetric residues go to the tensor-core kernel (ti_split_tc.cu) when `err` (the device
-// error word its bounded waits report to) is given and the layout suits its copies;
+// Residues go to the tensor-core kernel (ti_split_tc.cu) when `err` (the device error word
+// its bounded waits report to) is given and the layout suits its copies;
 // TI_SPLIT=simt keeps them on the SIMT kernels below, which give the same bytes, and
 // TI_SPLIT=tc reports an unsuitable layout as an error instead of falling back (tests).
 static int split_mode() {  // 0 simt, 1 tensor cores with fallback, 2 tensor cores only
@@ -270,7 +270,7 @@ cudaError_t launch_split(const double *X, int64_t outer, int64_t kdim, int64_t s
     if (outer == 0) return cudaSuccess;
     if (plane == 0) plane = outer * ld_res;
     const int64_t cap = int64_t(num_sms) * blocks_per_sm;
-    const int mode = (C.symmetric && err) ? split_mode() : 0;
+    const int mode = err ? split_mode() : 0;
     const bool try_tc = mode != 0;
     int tc_ctas = static_cast<int>(cap / 8);
     if (tc_ctas < 1) tc_ctas = 1;

@@ -14,9 +14,10 @@
 // (M = 128 rows = G groups x 128/G moduli slots, K = 8G bytes) times the digit matrix
 // B[(g', j)][n] = digit j of element (g', n) (N = 256).  D[(g, i)][n] = T_i of element (g, n)
 // lands in TMEM lane g * 128/G + i, so each epilogue thread owns one modulus of one group
-// and reduces consecutive elements of one vector:
+// and reduces consecutive elements of one vector, to the symmetric residue
 //   r = T - p * floor((T + h) / p)  in [-h, h],  h = (p - 1) / 2,
-// with the quotient umulhi(T + h, ceil(2^32 / p)), exact for T + h < 2^24.
+// or (kFloorMod) to the floor-mod residue r = T - p * floor(T / p) in [0, p), with the
+// quotient umulhi(T (+ h), ceil(2^32 / p)), exact for arguments below 2^24.
 //
 // G = 8 (up to 16 moduli; K = 64, two MMAs of K = 32) or G = 4 (up to 32 moduli; K = 32).
 // A unit is G vectors x 256 consecutive k: G rows of a k-contiguous operand or G columns of
@@ -27,9 +28,11 @@
 // Roles (one CTA per SM, persistent over units; vector blocks outer, k blocks fastest):
 //   warp 0       TMA producer: float64 tiles, 4-stage ring.
 //   warp 1       TMEM allocator (512 columns) + MMA issuer, 2 accumulators of 256 columns.
-//   warps 2..5   digits: scale each element, split it into 8 digits, store the B operand
-//                (2-stage ring).
-//   warps 6..13  epilogue: warp w reads TMEM lane quadrant w % 4, column half (w - 6) / 4.
+//   warps 2..9   digits: scale each element, split it into 8 digits, store the B operand
+//                (2-stage ring); two groups of four warps take alternate units.
+//   warps 10..25 epilogue: warp w reads TMEM lane quadrant w % 4, column quarter
+//                (w - 10) / 4; its 32 rows x 64 bytes pass through a private shared-memory
+//                tile so that each store writes whole 64-byte row segments.
 // Every wait is bounded; on timeout the CTA raises an error word, drains its in-flight
 // copies and MMAs, frees TMEM and exits.
 #include <atomic>
@@ -38,6 +41,9 @@
 #include "ti_scale.cuh"
 
 namespace ti {
+
+constexpr int kSpStagePitch = 80;                      // bytes per staged epilogue row
+constexpr int kSpStageWarpBytes = 32 * kSpStagePitch;  // one epilogue warp's 32 rows
 
 template <int kG>
 struct SplitTcCfg {
@@ -51,15 +57,16 @@ struct SplitTcCfg {
     static constexpr int kWBytes = 128 * kK;         // weights
     static constexpr uint32_t kSbo = kK * 8;         // stride of 8-row groups
     static constexpr int kPairs = kG;                // element pairs per digit thread per unit
-    static constexpr size_t kUsed =
-        size_t(kXStages) * kXBytes + size_t(kBStages) * kBBytes + kWBytes + 1024 + 256;
+    static constexpr size_t kUsed = size_t(kXStages) * kXBytes + size_t(kBStages) * kBBytes +
+                                    kWBytes + 16 * kSpStageWarpBytes + 1024 + 256;
     // at least 120 KB, so a second CTA (of this kernel, which takes all 512 TMEM columns)
     // never lands on the same SM and waits for TMEM
     static constexpr size_t kSmem = kUsed > 120 * 1024 ? kUsed : 120 * 1024;
 };
 
-constexpr int kSpDigitThreads = 128, kSpEpiThreads = 256;
-constexpr int kSpThreads = 64 + kSpDigitThreads + kSpEpiThreads;  // 448
+constexpr int kSpDigitThreads = 128;  // per group; two groups alternate units
+constexpr int kSpEpiThreads = 512;
+constexpr int kSpThreads = 64 + 2 * kSpDigitThreads + kSpEpiThreads;  // 832
 constexpr uint32_t kSpTmemCols = 512;
 constexpr uint32_t kSpIdesc = make_idesc_u8(128, 256);
 
@@ -112,7 +119,7 @@ __device__ __forceinline__ uint64_t digits8(double x, int bits, int e) {
     return (static_cast<uint64_t>(v) & 0x00FFFFFFFFFFFFFFull) | (v < 0 ? (1ull << 56) : 0ull);
 }
 
-template <int kG, bool kRows>
+template <int kG, bool kRows, bool kFloorMod>
 __global__ void __launch_bounds__(kSpThreads, 1)
     split_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ SplitTcParams P) {
     using Cfg = SplitTcCfg<kG>;
@@ -123,7 +130,8 @@ __global__ void __launch_bounds__(kSpThreads, 1)
     uint8_t *sW = smem;
     uint8_t *sB = sW + Cfg::kWBytes;
     uint8_t *sX = sB + Cfg::kBStages * Cfg::kBBytes;
-    uint64_t *xfull = reinterpret_cast<uint64_t *>(sX + Cfg::kXStages * Cfg::kXBytes);
+    uint8_t *sE = sX + Cfg::kXStages * Cfg::kXBytes;  // epilogue staging, per warp
+    uint64_t *xfull = reinterpret_cast<uint64_t *>(sE + 16 * kSpStageWarpBytes);
     uint64_t *xempty = xfull + Cfg::kXStages;
     uint64_t *bfull = xempty + Cfg::kXStages;
     uint64_t *bempty = bfull + Cfg::kBStages;
@@ -254,12 +262,17 @@ __global__ void __launch_bounds__(kSpThreads, 1)
                 sp_drain_wait(P, drain, 0);
             }
         }
-    } else if (warp < 6) {
-        // ---------------- digits (warps 2..5) ----------------
-        const int dt = threadIdx.x - 64;
-        int xs = 0, bs = 0;
-        uint32_t xph = 0, bph = 0;
-        for (GridIter it(P.k_blocks); it.a < P.vec_blocks; it.next()) {
+    } else if (warp < 10) {
+        // ---------------- digits (warps 2..9) ----------------
+        const int group = (warp - 2) >> 2;                     // takes units j with j % 2 == group
+        const int dt = (threadIdx.x - 64) & (kSpDigitThreads - 1);
+        int64_t j = 0;
+        for (GridIter it(P.k_blocks); it.a < P.vec_blocks; it.next(), ++j) {
+            if ((j & 1) != group) continue;
+            const int xs = static_cast<int>(j % Cfg::kXStages);
+            const uint32_t xph = static_cast<uint32_t>((j / Cfg::kXStages) & 1);
+            const int bs = static_cast<int>(j % Cfg::kBStages);
+            const uint32_t bph = static_cast<uint32_t>((j / Cfg::kBStages) & 1);
             const int64_t o0 = it.a * kG, l0 = it.b * Cfg::kN;
             if (!mbar_wait(&xfull[xs], xph, abort) || !mbar_wait(&bempty[bs], bph ^ 1, abort)) {
                 sp_raise(P, abort, kErrTimeoutEpilogue);
@@ -268,7 +281,7 @@ __global__ void __launch_bounds__(kSpThreads, 1)
             const double *X = reinterpret_cast<const double *>(sX + xs * Cfg::kXBytes);
             uint8_t *Bt = sB + bs * Cfg::kBBytes;
             const bool live = l0 < P.kdim;
-            // exponents of the groups this thread touches: all kG (rows: a = j / 2) or the
+            // exponents of the groups this thread touches: all kG (rows: a = jp / 2) or the
             // pair 2a, 2a+1 with a = dt % (kG/2) fixed (columns)
             int ex[kG];
 #pragma unroll
@@ -277,9 +290,9 @@ __global__ void __launch_bounds__(kSpThreads, 1)
                 ex[g] = (mine && o0 + g < P.outer) ? __ldg(P.exps + o0 + g) : kNonfiniteExp;
             }
 #pragma unroll
-            for (int j = 0; j < Cfg::kPairs; ++j) {
+            for (int jp = 0; jp < Cfg::kPairs; ++jp) {
                 // element pair (groups 2a and 2a+1, column n): 16 bytes of one B row
-                const int pi = dt + kSpDigitThreads * j;
+                const int pi = dt + kSpDigitThreads * jp;
                 const int a = kRows ? (pi >> 8) : (pi % (kG / 2));
                 const int n = kRows ? (pi & 255) : (pi / (kG / 2));
                 uint64_t d0 = 0, d1 = 0;
@@ -294,9 +307,9 @@ __global__ void __launch_bounds__(kSpThreads, 1)
                         x1 = v.y;
                     }
                     int e0, e1;
-                    if (kRows) {  // a is a compile-time function of j
-                        e0 = ex[2 * (j >> 1)];
-                        e1 = ex[2 * (j >> 1) + 1];
+                    if (kRows) {  // a is a compile-time function of jp
+                        e0 = ex[2 * (jp >> 1)];
+                        e1 = ex[2 * (jp >> 1) + 1];
                     } else {      // a = dt % (kG/2) for every j
                         e0 = kNonfiniteExp;
                         e1 = kNonfiniteExp;
@@ -317,24 +330,29 @@ __global__ void __launch_bounds__(kSpThreads, 1)
             fence_proxy_async_smem();  // digit stores before the tensor core reads them
             mbar_arrive(&xempty[xs]);
             mbar_arrive(&bfull[bs]);
-            if (++xs == Cfg::kXStages) {
-                xs = 0;
-                xph ^= 1;
-            }
-            if (++bs == Cfg::kBStages) {
-                bs = 0;
-                bph ^= 1;
-            }
         }
     } else {
-        // ---------------- epilogue (warps 6..13) ----------------
-        const int q = warp & 3;              // TMEM lane quadrant this warp may access
-        const int half = (warp - 6) >> 2;    // column half of the unit
-        const int L = q * 32 + lane;         // TMEM lane = weight row
-        const int g = L / Cfg::kSlots, i = L - g * Cfg::kSlots;
-        const bool mod_ok = i < P.n_mod;
-        const uint32_t p = mod_ok ? P.p[i] : 3u, h = p >> 1;
+        // ---------------- epilogue (warps 10..25) ----------------
+        const int q = warp & 3;                // TMEM lane quadrant this warp may access
+        const int quarter = (warp - 10) >> 2;  // 64-column quarter of the unit
+        const uint32_t p = (q * 32 + lane) % Cfg::kSlots < P.n_mod
+                               ? P.p[(q * 32 + lane) % Cfg::kSlots] : 3u;
+        const uint32_t h = kFloorMod ? 0u : (p >> 1);
         const uint32_t magic = static_cast<uint32_t>(((uint64_t(1) << 32) + p - 1) / p);
+        uint8_t *stage = sE + (warp - 10) * kSpStageWarpBytes;
+        // store phase: lane writes 16 bytes of staged row rr = 8*jj + lane/4 for jj = 0..3;
+        // row rr holds TMEM lane q*32 + rr = weight row (g, i)
+        int64_t roff[4];
+        int rg[4];
+        bool rok[4];
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+            const int Lr = q * 32 + 8 * jj + (lane >> 2);
+            const int gr = Lr / Cfg::kSlots, ir = Lr - gr * Cfg::kSlots;
+            rg[jj] = gr;
+            rok[jj] = ir < P.n_mod;
+            roff[jj] = int64_t(ir) * P.plane + int64_t(gr) * P.ld_res + (lane & 3) * 16;
+        }
         int64_t local = 0;
         for (GridIter it(P.k_blocks); it.a < P.vec_blocks; it.next(), ++local) {
             const int acc = static_cast<int>(local & 1);
@@ -344,23 +362,17 @@ __global__ void __launch_bounds__(kSpThreads, 1)
                 break;
             }
             tc_fence_after();
-            const int64_t o = it.a * kG + g;
-            const int64_t l0 = it.b * Cfg::kN + half * 128;
-            const bool active = mod_ok && o < P.outer;
-            int8_t *dst = P.res + (active ? int64_t(i) * P.plane + o * P.ld_res + l0 : 0);
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                                   static_cast<uint32_t>(acc) * 256u + half * 128;
+                                   static_cast<uint32_t>(acc) * 256u + quarter * 64;
 #pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < 2; ++c) {
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(tbase + c * 32, v);
                 tmem_wait_ld();
-                if (c == 3) {  // the accumulator is fully read
+                if (c == 1) {  // the accumulator is fully read
                     tc_fence_before();
                     mbar_arrive(&tempty[acc]);
                 }
-                const int64_t lc = l0 + c * 32;
-                if (!active || lc >= P.ld_res) continue;
                 uint32_t pk[8];
 #pragma unroll
                 for (int w = 0; w < 8; ++w) {
@@ -368,16 +380,27 @@ __global__ void __launch_bounds__(kSpThreads, 1)
 #pragma unroll
                     for (int b = 0; b < 4; ++b) {
                         const uint32_t T = v[4 * w + b];
-                        r[b] = T - __umulhi(T + h, magic) * p;  // low byte: the residue
+                        r[b] = T - __umulhi(kFloorMod ? T : T + h, magic) * p;  // low byte
                     }
                     pk[w] = __byte_perm(__byte_perm(r[0], r[1], 0x0040),
                                         __byte_perm(r[2], r[3], 0x0040), 0x5410);
                 }
-                *reinterpret_cast<uint4 *>(dst + c * 32) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                if (lc + 16 < P.ld_res)
-                    *reinterpret_cast<uint4 *>(dst + c * 32 + 16) =
-                        make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                uint4 *row = reinterpret_cast<uint4 *>(stage + lane * kSpStagePitch + c * 32);
+                row[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                row[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
             }
+            __syncwarp();
+            const int64_t o0 = it.a * kG;
+            const int64_t l0 = it.b * Cfg::kN + quarter * 64 + (lane & 3) * 16;
+            const int64_t base = o0 * P.ld_res + it.b * Cfg::kN + quarter * 64;
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+                const uint4 val = *reinterpret_cast<const uint4 *>(
+                    stage + (8 * jj + (lane >> 2)) * kSpStagePitch + (lane & 3) * 16);
+                if (rok[jj] && o0 + rg[jj] < P.outer && l0 < P.ld_res)
+                    *reinterpret_cast<uint4 *>(P.res + base + roff[jj]) = val;
+            }
+            __syncwarp();  // the staged rows are read before the next unit overwrites them
         }
     }
 
@@ -390,14 +413,14 @@ __global__ void __launch_bounds__(kSpThreads, 1)
     }
 }
 
-template <int kG, bool kRows>
+template <int kG, bool kRows, bool kFloorMod>
 static cudaError_t launch_split_tc_t(const CUtensorMap &tm, const SplitTcParams &P, int num_sms,
                                      cudaStream_t stream) {
     static std::atomic<int> configured{-1};  // last device configured
     int dev = 0;
     cudaGetDevice(&dev);
     if (configured.load() != dev) {
-        const cudaError_t e = cudaFuncSetAttribute(split_tc_kernel<kG, kRows>,
+        const cudaError_t e = cudaFuncSetAttribute(split_tc_kernel<kG, kRows, kFloorMod>,
                                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                    static_cast<int>(SplitTcCfg<kG>::kSmem));
         if (e != cudaSuccess) return e;
@@ -405,12 +428,13 @@ static cudaError_t launch_split_tc_t(const CUtensorMap &tm, const SplitTcParams 
     }
     const int64_t units = P.vec_blocks * P.k_blocks;
     const int64_t grid = units < num_sms ? units : num_sms;
-    split_tc_kernel<kG, kRows><<<static_cast<unsigned>(grid), kSpThreads, SplitTcCfg<kG>::kSmem,
-                                 stream>>>(tm, P);
+    split_tc_kernel<kG, kRows, kFloorMod><<<static_cast<unsigned>(grid), kSpThreads,
+                                            SplitTcCfg<kG>::kSmem, stream>>>(tm, P);
     return cudaGetLastError();
 }
 
-// Symmetric residues of one operand (exponents already in `exps`) on the tensor cores.
+// Residues of one operand (exponents already in `exps`) on the tensor cores: symmetric, or
+// floor-mod in [0, p) as unsigned bytes when C.symmetric is 0.
 // X is outer vectors of kdim elements, element (o, l) at X[o*s_outer + l*s_k], with either
 // s_k == 1 (rows) or s_outer == 1 (columns).  Writes res[i*plane + o*ld_res + l] for
 // l < ld_res (zero for l >= kdim).  Returns cudaErrorNotSupported when the layout does not
@@ -422,7 +446,7 @@ cudaError_t launch_split_tc(const double *X, int64_t outer, int64_t kdim, int64_
     if (outer == 0) return cudaSuccess;
     const bool rows = (s_k == 1);
     const int64_t stride = rows ? s_outer : s_k;
-    if (!C.symmetric || C.n_mod > kMaxModuli || kdim < 1 ||
+    if (C.n_mod > kMaxModuli || kdim < 1 ||
         (reinterpret_cast<uintptr_t>(X) & 15) || (stride & 1) || stride < 2 ||
         stride >= (int64_t(1) << 36) || (!rows && s_outer != 1) || (ld_res & 15) ||
         (plane & 15) || (reinterpret_cast<uintptr_t>(res) & 15))
@@ -455,11 +479,16 @@ cudaError_t launch_split_tc(const double *X, int64_t outer, int64_t kdim, int64_
     P.n_mod = C.n_mod;
     P.err = err;
     for (int i = 0; i < C.n_mod; ++i) P.p[i] = C.mm.p[i];
-    if (G == 8)
-        return rows ? launch_split_tc_t<8, true>(tm, P, num_sms, stream)
-                    : launch_split_tc_t<8, false>(tm, P, num_sms, stream);
-    return rows ? launch_split_tc_t<4, true>(tm, P, num_sms, stream)
-                : launch_split_tc_t<4, false>(tm, P, num_sms, stream);
+#define TI_SPLIT_TC(GG, FM)                                                               \
+    return rows ? launch_split_tc_t<GG, true, FM>(tm, P, num_sms, stream)                 \
+                : launch_split_tc_t<GG, false, FM>(tm, P, num_sms, stream);
+    if (G == 8) {
+        if (C.symmetric) { TI_SPLIT_TC(8, false) }
+        TI_SPLIT_TC(8, true)
+    }
+    if (C.symmetric) { TI_SPLIT_TC(4, false) }
+    TI_SPLIT_TC(4, true)
+#undef TI_SPLIT_TC
 }
 
 }  // namespace ti
