@@ -37,9 +37,10 @@ sys.path.insert(0, str(ROOT))
 METRIC = "emulated FP64 GEMM TFLOP/s at 8192³, 1/2/4/8 B200; % of int8 TC peak"
 UNIT = "TFLOP/s"
 GRIDS = {1: (1, 1), 2: (1, 2), 4: (2, 2), 8: (2, 4)}
-# dram__bytes_read.sum + dram__bytes_write.sum of one residue-GEMM launch at 8192^3 (25 moduli),
-# from the ncu capture summarised in profiles/residue_gemm_8192.md; None until captured.
-GEMM_DRAM_BYTES_8192 = None
+# dram__bytes_read.sum + dram__bytes_write.sum of one residue-GEMM launch at 8192^3 with the 16
+# wide moduli (5,299,600,384 + 1,059,266,304 bytes), from the 1-pass ncu launch list summarised
+# in profiles/launches_crt_matmul_8192.md.
+GEMM_DRAM_BYTES_8192 = 6358866688
 
 
 def parse_args():
@@ -447,7 +448,8 @@ def run_ours(args):
     achieved = gemm_ops / (gemm_span * 1e-3) / 1e12
     roof = {"bound": "tensor", "kernel": "residue_gemm_kernel (K2, tcgen05 kind::i8)",
             "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-            "traffic": GEMM_DRAM_BYTES_8192 if (m, n, k) == (8192, 8192, 8192) else None,
+            "traffic": (GEMM_DRAM_BYTES_8192 if (m, n, k) == (8192, 8192, 8192) and n_mod == 16
+                        else None),
             "peak_source": peak_src + " (of measured)",
             "ops_per_step": gemm_ops, "gemm_span_ms_per_step": gemm_span,
             "solo_achieved": gemm_ops / (k2 * 1e-3) / 1e12, "solo_ms_per_launch": k2,
