@@ -226,6 +226,21 @@ int ti_crt_matmul_noalloc(const double *A, int64_t sa0, int64_t sa1, const doubl
  */
 int ti_device_error(int *code_out, int reset);
 
+/*
+ * The unblocked LU panel with partial pivoting of src/tensor_inv/lu.py:24-34 (the loop over
+ * k in [j, jb) inside `lu`), in one launch on `stream`: for each column k the first index p of
+ * max |W[i, k]| over i >= k, the swap of rows k and p of W (all n columns) and of piv[k], piv[p],
+ * then, if |W[k, k]| > 1e-15, W[i, k] /= W[k, k] and W[i, c] -= W[i, k] * W[k, c] (product
+ * rounded first) for i > k, k < c < jb.  Bit-identical to the reference's torch loop.
+ * W: n x n float64, row-major with leading dimension ldw >= n; piv: int64 [n] (device).
+ * jb - j <= 1024.  workspace: ti_lu_panel_workspace_size() bytes of device memory, 256-byte
+ * aligned (its first bytes are cleared on `stream` by the call).  Returns TI_ERR_CUDA if the
+ * cooperative launch fails; a grid barrier that runs out sets the device error word.
+ */
+int ti_lu_panel_workspace_size(size_t *bytes);
+int ti_lu_panel(double *W, int64_t ldw, int64_t n, int64_t j, int64_t jb, int64_t *piv,
+                void *workspace, size_t workspace_bytes, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

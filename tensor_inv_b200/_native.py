@@ -69,6 +69,8 @@ SIGNATURES = {
     "ti_crt_matmul_host": (_int, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i64, _i64,
                                   _int, _p, _sz, _p, _opt]),
     "ti_device_error": (_int, [ctypes.POINTER(_int), _int]),
+    "ti_lu_panel_workspace_size": (_int, [ctypes.POINTER(_sz)]),
+    "ti_lu_panel": (_int, [_p, _i64, _i64, _i64, _i64, _p, _p, _sz, _p]),
 }
 
 _lib = None
@@ -190,3 +192,18 @@ def crt_host_workspace_size(m: int, n: int, k: int, bits: int, opt: CrtOptions) 
     check("ti_crt_host_workspace_size",
           lib().ti_crt_host_workspace_size(m, n, k, bits, ctypes.byref(opt), ctypes.byref(out)))
     return out.value
+
+
+def lu_panel_workspace_size() -> int:
+    out = ctypes.c_size_t(0)
+    check("ti_lu_panel_workspace_size", lib().ti_lu_panel_workspace_size(ctypes.byref(out)))
+    return out.value
+
+
+def lu_panel(W, j: int, jb: int, piv, workspace, stream) -> None:
+    """The unblocked LU panel on columns [j, jb) of the row-major float64 CUDA tensor W, with
+    the int64 pivot vector piv, in one launch on `stream` (a torch.cuda.Stream)."""
+    n = W.shape[0]
+    check("ti_lu_panel", lib().ti_lu_panel(W.data_ptr(), W.stride(0), n, j, jb, piv.data_ptr(),
+                                           workspace.data_ptr(), workspace.numel(),
+                                           stream.cuda_stream))

@@ -7,7 +7,7 @@ trailing update ``W[jb:, jb:] -= crt_matmul(L21, L21.T)`` runs fused on CUDA
 
 import torch
 
-from tensor_inv_b200.crt_matmul import crt_matmul, crt_matmul_update
+from tensor_inv_b200.crt_matmul import caller_moduli, crt_matmul, crt_matmul_update
 
 
 def cholesky(A, block_size=64):
@@ -38,9 +38,10 @@ def cholesky(A, block_size=64):
 
             # trailing GEMM update via CRT (cholesky.py:33)
             L21 = L[jb:, j:jb]
-            if W.is_cuda and W.dtype == torch.float64:
-                crt_matmul_update(W[jb:, jb:], L21, L21.T, alpha=-1)
+            mods = caller_moduli(b)  # same bits as the reference's primes, fewer GEMMs
+            if W.is_cuda and W.dtype == torch.float64 and W.stride(1) == 1:
+                crt_matmul_update(W[jb:, jb:], L21, L21.T, alpha=-1, moduli=mods)
             else:
-                W[jb:, jb:] -= crt_matmul(L21, L21.T)
+                W[jb:, jb:] -= crt_matmul(L21, L21.T, moduli=mods)
 
     return L

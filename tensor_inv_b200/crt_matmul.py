@@ -240,6 +240,13 @@ def _crt_matmul_host(A, B, bits, opt, dev):
     return out
 
 
+def caller_moduli(k):
+    """The moduli set the callers (lu, cholesky, rsvd) use for an inner dimension k: the wide
+    set whenever it keeps every bit (outputs bit-identical to the reference's primes, with
+    about a third fewer residue GEMMs), else the reference's primes."""
+    return "wide" if 0 < k <= nat.TI_MAX_K_WIDE else None
+
+
 def crt_matmul_update(C, A, B, alpha=-1, *, moduli=None, n_moduli=None):
     """In-place ``C += alpha * crt_matmul(A, B)`` for alpha in {-1, +1}, C float64 CUDA.
 

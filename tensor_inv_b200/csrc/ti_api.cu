@@ -205,8 +205,9 @@ static bool make_magic(const int32_t *moduli, int n, ModMagic &mm) {
     return true;
 }
 
+// mult: a factor folded into every residue ((mult_i * x) mod p_i), or null for none.
 static bool make_split_const(const int32_t *moduli, int n_mod, int bits, bool symmetric,
-                             SplitConst &C) {
+                             const uint32_t *mult, SplitConst &C) {
     std::memset(&C, 0, sizeof(C));
     C.n_mod = n_mod;
     C.bits = bits;
@@ -214,10 +215,12 @@ static bool make_split_const(const int32_t *moduli, int n_mod, int bits, bool sy
     if (!make_magic(moduli, n_mod, C.mm)) return false;
     for (int i = 0; i < n_mod; ++i) {
         const uint64_t p = static_cast<uint32_t>(moduli[i]);
-        C.w32[i] = static_cast<uint32_t>((uint64_t(1) << 32) % p);
-        C.w16[i] = static_cast<uint32_t>((uint64_t(1) << 16) % p);
+        const uint64_t m = mult ? mult[i] % p : 1;
+        C.mult[i] = static_cast<uint32_t>(m);
+        C.w32[i] = static_cast<uint32_t>((((uint64_t(1) << 32) % p) * m) % p);
+        C.w16[i] = static_cast<uint32_t>((((uint64_t(1) << 16) % p) * m) % p);
         C.bigp[i] = static_cast<uint32_t>(p * (((uint64_t(1) << 30) + p - 1) / p));
-        C.offs[i] = static_cast<uint32_t>(p * ((uint64_t(549388288) + p - 1) / p));
+        C.offs[i] = static_cast<uint32_t>(p * ((uint64_t(568197120) + p - 1) / p));
     }
     return true;
 }
@@ -232,6 +235,18 @@ static bool floor_mod_residues(const Plan &P, int64_t k) {
     int64_t pmax = 0;
     for (int i = 0; i < P.n_mod; ++i) pmax = P.moduli[i] > pmax ? P.moduli[i] : pmax;
     return k * (pmax - 1) * (pmax - 1) <= (int64_t(1) << 31) - 256;
+}
+
+static bool make_crt_const(const int32_t *moduli, int n_mod, int bits, CrtConst &K);
+
+// Split constants of the matmul path: A's residues carry the CRT factor u_i (so the residue
+// GEMM writes t_i = (u_i A_i B_i) mod p_i with one reduction), B's are plain.
+static bool make_matmul_consts(const Plan &PL, int64_t k, SplitConst &SCA, SplitConst &SCB,
+                               CrtConst &KC) {
+    const bool sym = !floor_mod_residues(PL, k);
+    return make_crt_const(PL.moduli, PL.n_mod, PL.bits, KC) &&
+           make_split_const(PL.moduli, PL.n_mod, PL.bits, sym, KC.u, SCA) &&
+           make_split_const(PL.moduli, PL.n_mod, PL.bits, sym, nullptr, SCB);
 }
 
 // Pairwise-coprime moduli with product below 2^127 (so every lifted value fits 128 bits).
@@ -290,6 +305,18 @@ struct DevInfo {
     int num_sms;
     int *err;
 };
+
+static int device_info(DevInfo &d);
+
+// SM count and device error word of the current device, for kernels in other files.
+int device_context(int *num_sms, int **err) {
+    DevInfo d;
+    const int rc = device_info(d);
+    if (rc != TI_OK) return rc;
+    *num_sms = d.num_sms;
+    *err = d.err;
+    return TI_OK;
+}
 
 static int device_info(DevInfo &d) {
     int dev = 0;
@@ -507,7 +534,7 @@ int ti_crt_split(const double *X, int64_t outer, int64_t kdim, int64_t s_outer, 
     int rc = device_info(d);
     if (rc != TI_OK) return rc;
     SplitConst C;
-    if (!make_split_const(kPrimes, n_mod, bits, false, C)) return TI_ERR_INVALID_ARGUMENT;
+    if (!make_split_const(kPrimes, n_mod, bits, false, nullptr, C)) return TI_ERR_INVALID_ARGUMENT;
     // s_k == 1 selects the k-contiguous kernels (also for a 1-long outer stride)
     const int64_t sk = (s_k == 1) ? 1 : s_k;
     const int64_t so = (s_k == 1) ? s_outer : 1;
@@ -589,7 +616,8 @@ static void record(void *const *ev, int i, cudaStream_t s) {
 static int crt_matmul_banded(const double *A, int64_t sa0, int64_t sa1, const double *B,
                              int64_t sb0, int64_t sb1, double *C, int64_t ldc, int64_t m,
                              int64_t n, int64_t k, int out_mode, void *const *ev,
-                             cudaStream_t s, const CrtLayout &L, const SplitConst &SC,
+                             cudaStream_t s, const CrtLayout &L, const SplitConst &SCA,
+                             const SplitConst &SC,
                              const CrtConst &KC, const DevInfo &d, int bands, int64_t band_rows,
                              int32_t *rexp, int32_t *cexp, int8_t *ares, int8_t *bres,
                              uint8_t *R) {
@@ -606,9 +634,9 @@ static int crt_matmul_banded(const double *A, int64_t sa0, int64_t sa1, const do
         const int64_t rows = m - r0 < band_rows ? m - r0 : band_rows;
         const double *Ab = A + r0 * sa0;
         if (sa1 == 1)
-            return launch_split(Ab, rows, k, sa0, 1, SC, rexp + r0, ares + r0 * L.ldk, L.ldk,
+            return launch_split(Ab, rows, k, sa0, 1, SCA, rexp + r0, ares + r0 * L.ldk, L.ldk,
                                 d.num_sms, st, a_plane, bps, d.err);
-        return launch_split(Ab, rows, k, 1, sa1, SC, rexp + r0, ares + r0 * L.ldk, L.ldk,
+        return launch_split(Ab, rows, k, 1, sa1, SCA, rexp + r0, ares + r0 * L.ldk, L.ldk,
                             d.num_sms, st, a_plane, bps, d.err);
     };
     record(ev, 0, s);
@@ -635,7 +663,7 @@ static int crt_matmul_banded(const double *A, int64_t sa0, int64_t sa1, const do
             return TI_ERR_CUDA;
         e = launch_residue_gemm(ares + r0 * L.ldk, bres, rows, n, k, L.ldk, L.n_mod, SC.mm,
                                 R + r0 * L.ldr, L.ldr, 0, d.err, d.num_sms, P.hi, a_plane,
-                                b_plane, r_plane, KC.u, !SC.symmetric);
+                                b_plane, r_plane, nullptr, !SC.symmetric);
         if (e != cudaSuccess) return e == cudaErrorInvalidValue ? TI_ERR_NO_DEVICE : TI_ERR_CUDA;
         if (cudaEventRecord(P.gemm_done[b], P.hi) != cudaSuccess) return TI_ERR_CUDA;
         // lo: split of the next band, then the reconstruction of this one
@@ -708,14 +736,12 @@ int ti_crt_matmul_ex(const double *A, int64_t sa0, int64_t sa1, const double *B,
     int8_t *bres = reinterpret_cast<int8_t *>(ws + L.off_b);
     uint8_t *R = ws + L.off_r;
 
-    SplitConst SC;
+    SplitConst SCA, SC;
     CrtConst KC;
     const Plan &PL = L.plan;
     // the residue representative follows floor_mod_residues (the products mod p do not
     // depend on it; the stage entry ti_crt_split keeps the reference's floor-mod bytes)
-    if (!make_split_const(PL.moduli, PL.n_mod, PL.bits, !floor_mod_residues(PL, k), SC))
-        return TI_ERR_UNSUPPORTED;
-    if (!make_crt_const(PL.moduli, PL.n_mod, PL.bits, KC)) return TI_ERR_UNSUPPORTED;
+    if (!make_matmul_consts(PL, k, SCA, SC, KC)) return TI_ERR_UNSUPPORTED;
 
     int bands = opt && opt->bands > 0 ? opt->bands : auto_bands(m);
     if (bands > kMaxBands) bands = kMaxBands;
@@ -724,13 +750,13 @@ int ti_crt_matmul_ex(const double *A, int64_t sa0, int64_t sa1, const double *B,
     bands = static_cast<int>((m + band_rows - 1) / band_rows);
     if (bands > 1 && !use_fused(m, n))
         return crt_matmul_banded(A, sa0, sa1, B, sb0, sb1, C, ldc, m, n, k, out_mode, ev, s, L,
-                                 SC, KC, d, bands, band_rows, rexp, cexp, ares, bres, R);
+                                 SCA, SC, KC, d, bands, band_rows, rexp, cexp, ares, bres, R);
 
     // K1: A as m vectors along k (rows), B as n vectors along k (columns)
     cudaError_t e;
     record(ev, 0, s);
-    if (sa1 == 1) e = launch_split(A, m, k, sa0, 1, SC, rexp, ares, L.ldk, d.num_sms, s, 0, 8, d.err);
-    else e = launch_split(A, m, k, 1, sa1, SC, rexp, ares, L.ldk, d.num_sms, s, 0, 8, d.err);
+    if (sa1 == 1) e = launch_split(A, m, k, sa0, 1, SCA, rexp, ares, L.ldk, d.num_sms, s, 0, 8, d.err);
+    else e = launch_split(A, m, k, 1, sa1, SCA, rexp, ares, L.ldk, d.num_sms, s, 0, 8, d.err);
     if (e != cudaSuccess) return TI_ERR_CUDA;
     if (sb0 == 1) e = launch_split(B, n, k, sb1, 1, SC, cexp, bres, L.ldk, d.num_sms, s, 0, 8, d.err);
     else e = launch_split(B, n, k, 1, sb0, SC, cexp, bres, L.ldk, d.num_sms, s, 0, 8, d.err);
@@ -741,7 +767,9 @@ int ti_crt_matmul_ex(const double *A, int64_t sa0, int64_t sa1, const double *B,
         int64_t grid = gemm_output_tiles(m, n);
         if (grid > d.num_sms) grid = d.num_sms;
         if (grid > kFusedMaxCtas) grid = kFusedMaxCtas;
-        e = launch_fused_gemm_crt(ares, bres, m, n, k, L.ldk, KC, rexp, cexp, C, ldc, out_mode, R,
+        CrtConst KF = KC;  // A's residues already carry u_i: the epilogue multiplies by 1
+        for (int i = 0; i < KF.n_mod; ++i) KF.u[i] = 1;
+        e = launch_fused_gemm_crt(ares, bres, m, n, k, L.ldk, KF, rexp, cexp, C, ldc, out_mode, R,
                                   static_cast<int>(grid), d.err, s, !SC.symmetric);
         record(ev, 2, s);
         record(ev, 3, s);
@@ -750,7 +778,7 @@ int ti_crt_matmul_ex(const double *A, int64_t sa0, int64_t sa1, const double *B,
     }
     // K2: per-modulus residue GEMMs, mod-reduced to uint8 planes
     e = launch_residue_gemm(ares, bres, m, n, k, L.ldk, L.n_mod, SC.mm, R, L.ldr, 0, d.err,
-                            d.num_sms, s, 0, 0, 0, KC.u, !SC.symmetric);
+                            d.num_sms, s, 0, 0, 0, nullptr, !SC.symmetric);
     if (e != cudaSuccess) return e == cudaErrorInvalidValue ? TI_ERR_NO_DEVICE : TI_ERR_CUDA;
     // K3: exact CRT + inverse scaling
     record(ev, 2, s);
@@ -767,7 +795,8 @@ int ti_crt_matmul_ex(const double *A, int64_t sa0, int64_t sa1, const double *B,
 // the following bands.
 static int crt_band_compute(const double *A, int64_t sa0, int64_t sa1, const double *B,
                             int64_t sb0, int64_t sb1, double *C, int64_t ldc, int64_t rows,
-                            int64_t n, int64_t k, const CrtLayout &L, const SplitConst &SC,
+                            int64_t n, int64_t k, const CrtLayout &L, const SplitConst &SCA,
+                            const SplitConst &SC,
                             const CrtConst &KC, uint8_t *ws, cudaStream_t s, bool split_b,
                             const DevInfo &d) {
     int32_t *rexp = reinterpret_cast<int32_t *>(ws + L.off_rexp);
@@ -781,11 +810,11 @@ static int crt_band_compute(const double *A, int64_t sa0, int64_t sa1, const dou
         else e = launch_split(B, n, k, 1, sb0, SC, cexp, bres, L.ldk, d.num_sms, s, 0, 8, d.err);
         if (e != cudaSuccess) return TI_ERR_CUDA;
     }
-    if (sa1 == 1) e = launch_split(A, rows, k, sa0, 1, SC, rexp, ares, L.ldk, d.num_sms, s, 0, 8, d.err);
-    else e = launch_split(A, rows, k, 1, sa1, SC, rexp, ares, L.ldk, d.num_sms, s, 0, 8, d.err);
+    if (sa1 == 1) e = launch_split(A, rows, k, sa0, 1, SCA, rexp, ares, L.ldk, d.num_sms, s, 0, 8, d.err);
+    else e = launch_split(A, rows, k, 1, sa1, SCA, rexp, ares, L.ldk, d.num_sms, s, 0, 8, d.err);
     if (e != cudaSuccess) return TI_ERR_CUDA;
     e = launch_residue_gemm(ares, bres, rows, n, k, L.ldk, L.n_mod, SC.mm, R, L.ldr, 0, d.err,
-                            d.num_sms, s, 0, 0, 0, KC.u, !SC.symmetric);
+                            d.num_sms, s, 0, 0, 0, nullptr, !SC.symmetric);
     if (e != cudaSuccess) return e == cudaErrorInvalidValue ? TI_ERR_NO_DEVICE : TI_ERR_CUDA;
     e = launch_k3(R, L.ldr, rows * L.ldr, rows, n, rexp, cexp, C, ldc, TI_OUT_STORE, KC, d.err,
                   d.num_sms, s);
@@ -850,14 +879,9 @@ int ti_crt_matmul_host(const double *A, int64_t sa0, int64_t sa1, const double *
     CrtLayout L;
     rc = crt_layout(m, n, k, bits, opt, L);
     if (rc != TI_OK) return rc;
-    SplitConst SC;
+    SplitConst SCA, SC;
     CrtConst KC;
-    if (k > 0) {
-        if (!make_split_const(L.plan.moduli, L.plan.n_mod, L.plan.bits,
-                              !floor_mod_residues(L.plan, k), SC) ||
-            !make_crt_const(L.plan.moduli, L.plan.n_mod, L.plan.bits, KC))
-            return TI_ERR_UNSUPPORTED;
-    }
+    if (k > 0 && !make_matmul_consts(L.plan, k, SCA, SC, KC)) return TI_ERR_UNSUPPORTED;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return TI_ERR_CUDA;
     std::lock_guard<std::mutex> lock(g_pipe[dev].mu);
@@ -911,7 +935,7 @@ int ti_crt_matmul_host(const double *A, int64_t sa0, int64_t sa1, const double *
             if (cudaStreamWaitEvent(s, P.a_in[b], 0) != cudaSuccess) return TI_ERR_CUDA;
             // band b of C = A[r0:r0+rows] @ B, with B split only once (in the first band)
             rc = crt_band_compute(dA + r0 * da0, da0, da1, dB, db0, db1, dC + r0 * n, n, rows, n,
-                                  k, L, SC, KC, ws + off_ws, s, b == 0, d);
+                                  k, L, SCA, SC, KC, ws + off_ws, s, b == 0, d);
             if (rc != TI_OK) return rc;
         } else if (cudaMemsetAsync(dC + r0 * n, 0, sizeof(double) * rows * n, s) != cudaSuccess) {
             return TI_ERR_CUDA;  // empty sum

@@ -24,6 +24,7 @@ enum : int {
     kErrTimeoutMma = 0x102,
     kErrTimeoutEpilogue = 0x103,
     kErrTimeoutDrain = 0x104,
+    kErrTimeoutGridBarrier = 0x105,
 };
 
 // Exact reduction a mod p for a < 2^31 and 3 <= p < 256, p not a power of two:
@@ -59,12 +60,16 @@ struct SplitConst {
     int symmetric;  // 0: floor-mod residues in [0, p) (the reference's _residues);
                     // 1: symmetric residues in [-(p-1)/2, (p-1)/2] (moduli up to 255)
     ModMagic mm;
-    uint32_t w32[kMaxModuli];   // 2^32 mod p
-    uint32_t w16[kMaxModuli];   // 2^16 mod p
+    // Every residue is written as (mult * x) mod p: mult = 1 for the reference's residues; the
+    // matmul path folds the CRT factor u_i = M_i^-1 mod p_i into A's residues, so the residue
+    // GEMM's output is already t_i = (u_i * A_i B_i) mod p_i.
+    uint32_t mult[kMaxModuli];
+    uint32_t w32[kMaxModuli];   // (2^32 mod p) * mult mod p
+    uint32_t w16[kMaxModuli];   // (2^16 mod p) * mult mod p
     uint32_t bigp[kMaxModuli];  // p * ceil(2^30 / p): a multiple of p above any piece sum
-                                // (a2*w32 + a1*w16 + a0 < 2^21*255 + 2^16*255 + 2^16 < 2^30)
-    uint32_t offs[kMaxModuli];  // p * ceil(549388288 / p): a multiple of p above any |T|
-                                // (T = a2*w32 + a1*w16 + a0 of signed pieces, |T| < 549388288)
+                                // (a2*w32 + a1*w16 + a0*mult < 2^21*254 + 2*2^16*254 < 2^30)
+    uint32_t offs[kMaxModuli];  // p * ceil(568197120 / p): a multiple of p above any |T|
+                                // (T = a2*w32 + a1*w16 + a0*mult of signed pieces)
 };
 
 // Constants of the CRT reconstruction.  M = prod p_i < 2^127, M_i = M / p_i.

@@ -371,16 +371,27 @@ __global__ void __launch_bounds__(gemm_threads(kFused), 1)
                 } else if (row < P.m && col0 < P.ldo) {
                     if (!P.out_i32) {
                         uint32_t pk[8];
-                        const uint32_t wt = P.store_t ? P.crt.u[mod] : 1u;
+                        if (P.store_t) {  // t = (r * u) mod p
+                            const uint32_t wt = P.crt.u[mod];
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) {
-                            uint32_t w = 0;
+                            for (int j = 0; j < 8; ++j) {
+                                uint32_t w = 0;
 #pragma unroll
-                            for (int b = 0; b < 4; ++b) {
-                                const uint32_t r = mod_acc(v[4 * j + b], p, magic, shift, off);
-                                w |= mod_small(r * wt, p, magic, shift) << (8 * b);
+                                for (int b = 0; b < 4; ++b) {
+                                    const uint32_t r = mod_acc(v[4 * j + b], p, magic, shift, off);
+                                    w |= mod_small(r * wt, p, magic, shift) << (8 * b);
+                                }
+                                pk[j] = w;
                             }
-                            pk[j] = w;
+                        } else {  // r itself (the matmul path folds u into A's residues)
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) {
+                                uint32_t w = 0;
+#pragma unroll
+                                for (int b = 0; b < 4; ++b)
+                                    w |= mod_acc(v[4 * j + b], p, magic, shift, off) << (8 * b);
+                                pk[j] = w;
+                            }
                         }
                         uint8_t *dst = static_cast<uint8_t *>(P.out) + mod * P.plane + row * P.ldo + col0;
                         *reinterpret_cast<uint4 *>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);

@@ -1,0 +1,481 @@
+// ti_lu.cu -- the unblocked LU panel with partial pivoting as one cooperative kernel.
+//
+// Restates the panel loop of src/tensor_inv/lu.py:24-34 with the same IEEE operations in the
+// same order, so P, L and U are bit-identical to the reference's torch loop:
+//   for k in [j, jb):
+//     p = first index of the maximum of |W[i, k]| over i >= k    (torch argmax)
+//     if p != k: swap rows k and p of W (all n columns) and entries k and p of piv
+//     if |W[k, k]| > 1e-15:
+//       W[i, k] = W[i, k] / W[k, k]                            for i > k
+//       W[i, c] = W[i, c] - round(W[i, k] * W[k, c])           for i > k, k < c < jb
+// The product is rounded before the subtraction, as the reference's separate `@` (a K = 1
+// matrix product) and `-=`; nothing is contracted into a fused multiply-add.
+//
+// One launch per panel replaces the reference's 8 small launches and 2 host round trips per
+// column.  CTAs (launched cooperatively, so all are resident at once) own contiguous row
+// ranges of the panel.  Each column takes two grid barriers: after the per-CTA argmax
+// candidates (every CTA then reduces the same candidates in the same order, so all agree on
+// p), and after the row swap (the update reads the pivot row).  The barrier is a counter and
+// a generation word in the caller's workspace; every wait is bounded in time, and on timeout
+// the kernel records an error and all CTAs return.  All accesses to W bypass L1 (ld/st .cg), so
+// a CTA never reads a stale copy of a row that another CTA swapped or updated.
+#include <cstring>
+
+#include "tensor_inv_crt.h"
+#include "ti_common.cuh"
+
+namespace ti {
+
+int device_context(int *num_sms, int **err);
+
+constexpr int kLuThreads = 256;
+constexpr int kLuMaxCtas = 1024;
+constexpr int kLuMaxPanel = 1024;  // columns per panel
+
+struct LuSync {
+    unsigned count;
+    unsigned gen;
+    int abort;
+    int pad;
+};
+
+struct LuCand {
+    double v;   // |W[i, k]|
+    long long i;
+};
+
+// a is a better argmax candidate than b: larger, or NaN over a number, or equal with the
+// smaller index (torch.argmax returns the first maximal element; NaN counts as maximal)
+__device__ __forceinline__ bool lu_better(double av, long long ai, double bv, long long bi) {
+    const bool an = av != av, bn = bv != bv;
+    if (an != bn) return an;
+    if (!an && av != bv) return av > bv;
+    return ai < bi;
+}
+
+// Grid-wide barrier over `nblocks` co-resident CTAs.  Returns false (in every thread of the
+// CTA) if a wait ran out or another CTA gave up.
+__device__ bool lu_grid_sync(LuSync *s, unsigned nblocks, unsigned &gen_local, int *err) {
+    __shared__ int ok_sh;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int ok = 1;
+        const unsigned target = gen_local + 1;
+        __threadfence();  // this CTA's writes before its arrival
+        if (atomicAdd(&s->count, 1u) == nblocks - 1) {
+            atomicExch(&s->count, 0u);
+            __threadfence();
+            atomicExch(&s->gen, target);  // release everyone
+        } else {
+            const unsigned long long t0 = globaltimer_ns();
+            while (*reinterpret_cast<volatile unsigned *>(&s->gen) != target) {
+                if (*reinterpret_cast<volatile int *>(&s->abort)) {
+                    ok = 0;
+                    break;
+                }
+                if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+                    atomicExch(&s->abort, 1);
+                    atomicCAS(err, 0, kErrTimeoutGridBarrier);
+                    ok = 0;
+                    break;
+                }
+                __nanosleep(64);
+            }
+        }
+        __threadfence();  // the other CTAs' writes after the release
+        gen_local = target;
+        ok_sh = ok;
+    }
+    __syncthreads();
+    return ok_sh != 0;
+}
+
+// The global pivot from the G published candidates: thread t loads candidate t (all loads in
+// flight at once), then a warp and a block reduction.  Every CTA reduces the same values with
+// the same total order (value, then index), so all CTAs agree.  Returns the row in *row and the
+// publishing CTA in *cta (block-uniform, through shared memory).
+__device__ __forceinline__ void lu_global_pivot(const LuCand *cands, unsigned G, long long *row,
+                                                int *cta, double *red_v, long long *red_i,
+                                                int *red_b) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    double bv = -1.0;
+    long long bi = LLONG_MAX;
+    int bb = 0;
+    for (unsigned q = tid; q < G; q += kLuThreads) {
+        const double v = __ldcg(&cands[q].v);
+        const long long i = __ldcg(&cands[q].i);
+        if (i != LLONG_MAX && (bi == LLONG_MAX || lu_better(v, i, bv, bi))) {
+            bv = v;
+            bi = i;
+            bb = static_cast<int>(q);
+        }
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) {
+        const double ov = __shfl_xor_sync(0xFFFFFFFFu, bv, off);
+        const long long oi = __shfl_xor_sync(0xFFFFFFFFu, bi, off);
+        const int ob = __shfl_xor_sync(0xFFFFFFFFu, bb, off);
+        if (oi != LLONG_MAX && (bi == LLONG_MAX || lu_better(ov, oi, bv, bi))) {
+            bv = ov;
+            bi = oi;
+            bb = ob;
+        }
+    }
+    if (lane == 0) {
+        red_v[warp] = bv;
+        red_i[warp] = bi;
+        red_b[warp] = bb;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        for (int w = 1; w < kLuThreads / 32; ++w)
+            if (red_i[w] != LLONG_MAX && (bi == LLONG_MAX || lu_better(red_v[w], red_i[w], bv, bi))) {
+                bv = red_v[w];
+                bi = red_i[w];
+                bb = red_b[w];
+            }
+        *row = bi;
+        *cta = bb;
+    }
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(kLuThreads)
+    lu_panel_kernel(double *__restrict__ W, int64_t ldw, int64_t n, int64_t j, int64_t jb,
+                    int64_t *__restrict__ piv, LuSync *sync, LuCand *cand, int *err) {
+    __shared__ double urow[kLuMaxPanel];  // W[k, k+1 .. jb-1] of the current column
+    __shared__ double red_v[kLuThreads / 32];
+    __shared__ long long red_i[kLuThreads / 32];
+    __shared__ int red_b[kLuThreads / 32];
+    __shared__ long long piv_row;
+    __shared__ int piv_cta;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const unsigned G = gridDim.x;
+    const int64_t rows = n - j;
+    const int64_t per = (rows + G - 1) / G;
+    const int64_t r0 = j + int64_t(blockIdx.x) * per;
+    const int64_t r1 = r0 + per < n ? r0 + per : n;  // owned rows [r0, r1)
+    unsigned gen = 0;
+
+    for (int64_t k = j; k < jb; ++k) {
+        // ---- A: this CTA's argmax candidate over owned rows >= k (column k)
+        double bv = -1.0;
+        long long bi = LLONG_MAX;
+        for (int64_t i = (r0 > k ? r0 : k) + tid; i < r1; i += kLuThreads) {
+            const double v = fabs(__ldcg(W + i * ldw + k));
+            if (bi == LLONG_MAX || lu_better(v, i, bv, bi)) {
+                bv = v;
+                bi = i;
+            }
+        }
+#pragma unroll
+        for (int off = 16; off; off >>= 1) {
+            const double ov = __shfl_xor_sync(0xFFFFFFFFu, bv, off);
+            const long long oi = __shfl_xor_sync(0xFFFFFFFFu, bi, off);
+            if (oi != LLONG_MAX && (bi == LLONG_MAX || lu_better(ov, oi, bv, bi))) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (lane == 0) {
+            red_v[warp] = bv;
+            red_i[warp] = bi;
+        }
+        __syncthreads();
+        if (tid == 0) {
+            for (int w = 1; w < kLuThreads / 32; ++w)
+                if (red_i[w] != LLONG_MAX &&
+                    (bi == LLONG_MAX || lu_better(red_v[w], red_i[w], bv, bi))) {
+                    bv = red_v[w];
+                    bi = red_i[w];
+                }
+            cand[blockIdx.x].v = bv;
+            cand[blockIdx.x].i = bi;
+        }
+        if (!lu_grid_sync(sync, G, gen, err)) return;
+
+        // ---- B: the global pivot, then the row swap
+        lu_global_pivot(cand, G, &piv_row, &piv_cta, red_v, red_i, red_b);
+        const int64_t p = piv_row;
+        if (p != k) {
+            const int64_t per_c = (n + G - 1) / G;
+            const int64_t c0 = int64_t(blockIdx.x) * per_c;
+            const int64_t c1 = c0 + per_c < n ? c0 + per_c : n;
+            for (int64_t c = c0 + tid; c < c1; c += kLuThreads) {
+                const double a = __ldcg(W + k * ldw + c), b = __ldcg(W + p * ldw + c);
+                __stcg(W + k * ldw + c, b);
+                __stcg(W + p * ldw + c, a);
+            }
+            if (blockIdx.x == 0 && tid == 0) {
+                const int64_t t = piv[k];
+                piv[k] = piv[p];
+                piv[p] = t;
+            }
+        }
+        if (!lu_grid_sync(sync, G, gen, err)) return;
+
+        // ---- C: scale column k and update the panel, owned rows > k
+        const double d = __ldcg(W + k * ldw + k);
+        if (!(fabs(d) > 1e-15)) continue;  // the reference skips this column
+        const int64_t nc = jb - k - 1;
+        for (int64_t c = tid; c < nc; c += kLuThreads) urow[c] = __ldcg(W + k * ldw + k + 1 + c);
+        __syncthreads();
+        for (int64_t i = (r0 > k + 1 ? r0 : k + 1) + warp; i < r1; i += kLuThreads / 32) {
+            double *wi = W + i * ldw;
+            const double l = __ddiv_rn(__ldcg(wi + k), d);
+            for (int64_t c0 = 0; c0 < nc; c0 += 256) {  // 8 loads in flight per lane
+                double x[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int64_t c = c0 + lane + 32 * u;
+                    x[u] = c < nc ? __ldcg(wi + k + 1 + c) : 0.0;
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int64_t c = c0 + lane + 32 * u;
+                    if (c < nc) __stcg(wi + k + 1 + c, __dsub_rn(x[u], __dmul_rn(l, urow[c])));
+                }
+            }
+            if (lane == 0) __stcg(wi + k, l);
+        }
+        __syncthreads();  // urow is rewritten in the next column
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// Shared-memory variant: each CTA keeps its panel rows (all b columns) in shared memory for
+// the whole panel, so the column updates never touch global memory, and one grid barrier per
+// column suffices.  Before the barrier every CTA publishes its argmax candidate and that
+// candidate's panel row, and the owner of row k publishes row k (double-buffered by column
+// parity: a CTA can only write column k+1's slots after every CTA has passed column k's
+// barrier, and it reads column k's slots before arriving at column k+1's).  After the barrier
+// every CTA takes the pivot row from the winner's slot; the owners of rows k and p swap their
+// panel parts from the slots, and the columns outside the panel are swapped in global memory
+// (each CTA always takes the same column slice, so its swaps stay in program order).
+// ---------------------------------------------------------------------------------------
+constexpr int kLuSmemMaxPanel = 256;
+constexpr int kLuSmemMaxCtas = 256;
+
+struct LuSlots {
+    LuCand cand[2][kLuSmemMaxCtas];
+    double krow[2][kLuSmemMaxPanel];
+    double crow[2][kLuSmemMaxCtas][kLuSmemMaxPanel];
+};
+
+__global__ void __launch_bounds__(kLuThreads)
+    lu_panel_smem_kernel(double *__restrict__ W, int64_t ldw, int64_t n, int64_t j, int64_t jb,
+                         int64_t *__restrict__ piv, LuSync *sync, LuSlots *slots, int *err) {
+    extern __shared__ double P[];            // [per][b + 1]: owned rows, panel columns
+    __shared__ double urow[kLuSmemMaxPanel];  // the pivot row (after the swap), panel columns
+    __shared__ double red_v[kLuThreads / 32];
+    __shared__ long long red_i[kLuThreads / 32];
+    __shared__ int red_b[kLuThreads / 32];
+    __shared__ long long piv_row;
+    __shared__ int piv_cta;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const unsigned G = gridDim.x;
+    const int b = static_cast<int>(jb - j), pitch = b + 1;
+    const int64_t per = (n - j + G - 1) / G;
+    const int64_t r0 = j + int64_t(blockIdx.x) * per;
+    const int64_t r1 = r0 + per < n ? r0 + per : n;
+    const int nr = r1 > r0 ? static_cast<int>(r1 - r0) : 0;
+    unsigned gen = 0;
+
+    for (int e = tid; e < nr * b; e += kLuThreads) {
+        const int r = e / b, c = e - r * b;
+        P[r * pitch + c] = __ldcg(W + (r0 + r) * ldw + j + c);
+    }
+    // columns outside the panel, this CTA's slice of them (for the row swaps)
+    const int64_t nout = n - b;
+    const int64_t per_c = (nout + G - 1) / G;
+    const int64_t t0 = int64_t(blockIdx.x) * per_c;
+    const int64_t t1 = t0 + per_c < nout ? t0 + per_c : nout;
+    __syncthreads();
+
+    for (int64_t k = j; k < jb; ++k) {
+        const int kc = static_cast<int>(k - j);  // panel column of k
+        const int par = static_cast<int>(k & 1);
+        // ---- A: candidate over owned rows >= k; publish it and (owner of k) row k
+        double bv = -1.0;
+        long long bi = LLONG_MAX;
+        for (int64_t i = (r0 > k ? r0 : k) + tid; i < r1; i += kLuThreads) {
+            const double v = fabs(P[(i - r0) * pitch + kc]);
+            if (bi == LLONG_MAX || lu_better(v, i, bv, bi)) {
+                bv = v;
+                bi = i;
+            }
+        }
+#pragma unroll
+        for (int off = 16; off; off >>= 1) {
+            const double ov = __shfl_xor_sync(0xFFFFFFFFu, bv, off);
+            const long long oi = __shfl_xor_sync(0xFFFFFFFFu, bi, off);
+            if (oi != LLONG_MAX && (bi == LLONG_MAX || lu_better(ov, oi, bv, bi))) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (lane == 0) {
+            red_v[warp] = bv;
+            red_i[warp] = bi;
+        }
+        __syncthreads();
+        if (tid == 0) {
+            for (int w = 1; w < kLuThreads / 32; ++w)
+                if (red_i[w] != LLONG_MAX &&
+                    (bi == LLONG_MAX || lu_better(red_v[w], red_i[w], bv, bi))) {
+                    bv = red_v[w];
+                    bi = red_i[w];
+                }
+            slots->cand[par][blockIdx.x].v = bv;
+            slots->cand[par][blockIdx.x].i = bi;
+            piv_row = bi;
+        }
+        __syncthreads();
+        const long long mine = piv_row;
+        if (mine != LLONG_MAX)
+            for (int c = tid; c < b; c += kLuThreads)
+                __stcg(&slots->crow[par][blockIdx.x][c], P[(mine - r0) * pitch + c]);
+        if (k >= r0 && k < r1)
+            for (int c = tid; c < b; c += kLuThreads)
+                __stcg(&slots->krow[par][c], P[(k - r0) * pitch + c]);
+        if (!lu_grid_sync(sync, G, gen, err)) return;
+
+        // ---- B: the global pivot, the pivot row, the swap
+        lu_global_pivot(slots->cand[par], G, &piv_row, &piv_cta, red_v, red_i, red_b);
+        const int64_t p = piv_row;
+        const int pc = piv_cta;
+        for (int c = tid; c < b; c += kLuThreads) urow[c] = __ldcg(&slots->crow[par][pc][c]);
+        if (p != k) {
+            if (k >= r0 && k < r1)  // row k takes old row p
+                for (int c = tid; c < b; c += kLuThreads)
+                    P[(k - r0) * pitch + c] = __ldcg(&slots->crow[par][pc][c]);
+            if (p >= r0 && p < r1)  // row p takes old row k
+                for (int c = tid; c < b; c += kLuThreads)
+                    P[(p - r0) * pitch + c] = __ldcg(&slots->krow[par][c]);
+            for (int64_t t = t0 + tid; t < t1; t += kLuThreads) {
+                const int64_t c = t < j ? t : t + b;
+                const double x = __ldcg(W + k * ldw + c), y = __ldcg(W + p * ldw + c);
+                __stcg(W + k * ldw + c, y);
+                __stcg(W + p * ldw + c, x);
+            }
+            if (blockIdx.x == 0 && tid == 0) {
+                const int64_t t = piv[k];
+                piv[k] = piv[p];
+                piv[p] = t;
+            }
+        }
+        __syncthreads();
+
+        // ---- C: scale and update owned rows > k in shared memory
+        const double d = urow[kc];
+        if (fabs(d) > 1e-15) {
+            for (int64_t i = (r0 > k + 1 ? r0 : k + 1) + warp; i < r1; i += kLuThreads / 32) {
+                double *pi = P + (i - r0) * pitch;
+                const double l = __ddiv_rn(pi[kc], d);
+                for (int c = kc + 1 + lane; c < b; c += 32)
+                    pi[c] = __dsub_rn(pi[c], __dmul_rn(l, urow[c]));
+                __syncwarp();
+                if (lane == 0) pi[kc] = l;
+            }
+        }
+        __syncthreads();
+    }
+
+    for (int e = tid; e < nr * b; e += kLuThreads) {
+        const int r = e / b, c = e - r * b;
+        __stcg(W + (r0 + r) * ldw + j + c, P[r * pitch + c]);
+    }
+}
+
+size_t lu_smem_bytes(int64_t rows_per_cta, int64_t b) {
+    return size_t(rows_per_cta) * size_t(b + 1) * sizeof(double);
+}
+
+}  // namespace ti
+
+using namespace ti;
+
+extern "C" {
+
+// Workspace: the barrier words (256 bytes), the candidates of the global-memory kernel, then
+// the slots of the shared-memory kernel.
+static size_t lu_cand_offset() { return 256; }
+static size_t lu_slots_offset() {
+    return (256 + sizeof(LuCand) * kLuMaxCtas + 255) / 256 * 256;
+}
+
+int ti_lu_panel_workspace_size(size_t *bytes) {
+    if (!bytes) return TI_ERR_INVALID_ARGUMENT;
+    *bytes = lu_slots_offset() + sizeof(LuSlots);
+    return TI_OK;
+}
+
+int ti_lu_panel(double *W, int64_t ldw, int64_t n, int64_t j, int64_t jb, int64_t *piv,
+                void *workspace, size_t workspace_bytes, void *stream) {
+    if (!W || !piv || n < 1 || ldw < n || j < 0 || jb <= j || jb > n ||
+        jb - j > kLuMaxPanel)
+        return TI_ERR_INVALID_ARGUMENT;
+    size_t need = 0;
+    ti_lu_panel_workspace_size(&need);
+    if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255))
+        return TI_ERR_WORKSPACE;
+    int num_sms = 0;
+    int *err = nullptr;
+    int rc = device_context(&num_sms, &err);
+    if (rc != TI_OK) return rc;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, lu_panel_kernel, kLuThreads, 0) !=
+            cudaSuccess ||
+        per_sm < 1)
+        return TI_ERR_CUDA;
+    // at least 32 rows per CTA; every CTA resident at once (cooperative launch)
+    int64_t grid = (n - j + 31) / 32;
+    if (grid > num_sms) grid = num_sms;
+    if (grid > int64_t(per_sm) * num_sms) grid = int64_t(per_sm) * num_sms;
+    if (grid > kLuMaxCtas) grid = kLuMaxCtas;
+    if (grid < 1) grid = 1;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    LuSync *sync = reinterpret_cast<LuSync *>(ws);
+    if (cudaMemsetAsync(sync, 0, sizeof(LuSync), s) != cudaSuccess) return TI_ERR_CUDA;
+    // shared-memory variant when the CTAs' panel rows fit (one CTA per SM)
+    const int64_t b = jb - j;
+    int64_t g_smem = (n - j + 31) / 32;
+    if (g_smem > num_sms) g_smem = num_sms;
+    if (g_smem > kLuSmemMaxCtas) g_smem = kLuSmemMaxCtas;
+    const int64_t per = (n - j + g_smem - 1) / g_smem;
+    const size_t smem = lu_smem_bytes(per, b);
+    if (b <= kLuSmemMaxPanel && smem <= size_t(200) * 1024) {
+        static int configured = -1;
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (configured != dev) {
+            if (cudaFuncSetAttribute(lu_panel_smem_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     200 * 1024) != cudaSuccess)
+                return TI_ERR_CUDA;
+            configured = dev;
+        }
+        int per_sm_s = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_s, lu_panel_smem_kernel,
+                                                          kLuThreads, smem) == cudaSuccess &&
+            int64_t(per_sm_s) * num_sms >= g_smem) {
+            LuSlots *slots = reinterpret_cast<LuSlots *>(ws + lu_slots_offset());
+            void *args[] = {&W, &ldw, &n, &j, &jb, &piv, &sync, &slots, &err};
+            if (cudaLaunchCooperativeKernel(reinterpret_cast<const void *>(lu_panel_smem_kernel),
+                                            dim3(static_cast<unsigned>(g_smem)), dim3(kLuThreads),
+                                            args, smem, s) != cudaSuccess)
+                return TI_ERR_CUDA;
+            return TI_OK;
+        }
+    }
+    LuCand *cand = reinterpret_cast<LuCand *>(ws + lu_cand_offset());
+    void *args[] = {&W, &ldw, &n, &j, &jb, &piv, &sync, &cand, &err};
+    if (cudaLaunchCooperativeKernel(reinterpret_cast<const void *>(lu_panel_kernel),
+                                    dim3(static_cast<unsigned>(grid)), dim3(kLuThreads), args, 0,
+                                    s) != cudaSuccess)
+        return TI_ERR_CUDA;
+    return TI_OK;
+}
+
+}  // extern "C"

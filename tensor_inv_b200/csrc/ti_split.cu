@@ -25,12 +25,12 @@ __device__ __forceinline__ uint2 residues8(const uint32_t (&a2)[8], const uint32
                                            const uint32_t (&a0)[8], uint32_t negmask,
                                            const SplitConst &C, int i) {
     const uint32_t p = C.mm.p[i], magic = C.mm.magic[i], shift = C.mm.shift[i];
-    const uint32_t w32 = C.w32[i], w16 = C.w16[i], bigp = C.bigp[i];
+    const uint32_t w32 = C.w32[i], w16 = C.w16[i], bigp = C.bigp[i], mult = C.mult[i];
     uint32_t out[2] = {0u, 0u};
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-        // mag = a2*2^32 + a1*2^16 + a0  ==>  t == mag (mod p), t < 2^30
-        uint32_t t = a2[j] * w32 + a1[j] * w16 + a0[j];
+        // mag = a2*2^32 + a1*2^16 + a0  ==>  t == mult * mag (mod p), t < 2^30
+        uint32_t t = a2[j] * w32 + a1[j] * w16 + a0[j] * mult;
         t = ((negmask >> j) & 1u) ? bigp - t : t;  // -mag (mod p), bigp - t < 2^31
         const uint32_t r = mod_small(t, p, magic, shift);
         out[j >> 2] |= r << (8 * (j & 3));
@@ -39,18 +39,19 @@ __device__ __forceinline__ uint2 residues8(const uint32_t (&a2)[8], const uint32
 }
 
 // Symmetric residues of 8 signed values given as signed pieces (v = a2*2^32 + a1*2^16 + a0
-// with every piece carrying the sign of v): T = a2*w32 + a1*w16 + a0 == v (mod p) with
-// |T| < 549388288; u = T + offs (a multiple of p above |T|, so 0 <= u < 2^31);
+// with every piece carrying the sign of v): T = a2*w32 + a1*w16 + a0*mult == mult*v (mod p)
+// with |T| < 568197120; u = T + offs (a multiple of p above |T|, so 0 <= u < 2^31);
 // q = floor((u + h) / p) exactly, and u - q*p is the residue in [-h, h], h = (p-1)/2.
 __device__ __forceinline__ uint2 residues8_sym(const uint32_t (&a2)[8], const uint32_t (&a1)[8],
                                                const uint32_t (&a0)[8], const SplitConst &C,
                                                int i) {
     const uint32_t p = C.mm.p[i], magic = C.mm.magic[i], shift = C.mm.shift[i];
     const uint32_t w32 = C.w32[i], w16 = C.w16[i], offs = C.offs[i], h = p >> 1;
+    const uint32_t mult = C.mult[i];
     uint32_t r[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-        const uint32_t u = a2[j] * w32 + a1[j] * w16 + (a0[j] + offs);
+        const uint32_t u = a2[j] * w32 + a1[j] * w16 + (a0[j] * mult + offs);
         const uint32_t q = __umulhi(u + h, magic) >> shift;
         r[j] = u - q * p;  // low byte is the two's-complement residue
     }

@@ -7,8 +7,9 @@
 // Per element the scaled integer v = round_half_even(x * 2^(bits - e)), |v| <= 2^53, is
 // written as eight unsigned digits: b_0..b_6, the bytes of v mod 2^56, and b_7 = [v < 0], so
 //   v = sum_{j<7} b_j 2^(8j) - 2^56 b_7.
-// With c_(j,i) = 2^(8j) mod p_i (j < 7) and c_(7,i) = (-2^56) mod p_i, all in [0, p_i),
-//   T_i = sum_j b_j c_(j,i) == v (mod p_i),   0 <= T_i < 8 * 255 * 255 < 2^19,
+// With c_(j,i) = m_i 2^(8j) mod p_i (j < 7) and c_(7,i) = -m_i 2^56 mod p_i, all in [0, p_i)
+// (m_i the factor folded into the residues, 1 for plain ones),
+//   T_i = sum_j b_j c_(j,i) == m_i v (mod p_i),   0 <= T_i < 8 * 255 * 255 < 2^19,
 // an unsigned 8-bit matrix product with 32-bit accumulation.  G element groups share one
 // MMA through a block-diagonal weight matrix W[(g, i)][(g', j)] = [g == g'] c_(j,i)
 // (M = 128 rows = G groups x 128/G moduli slots, K = 8G bytes) times the digit matrix
@@ -78,6 +79,7 @@ struct SplitTcParams {
     int bits, n_mod;
     int *err;
     uint32_t p[kMaxModuli];
+    uint32_t mult[kMaxModuli];  // factor folded into every residue (1: none)
 };
 
 __device__ __forceinline__ void sp_raise(const SplitTcParams &P, volatile int *abort, int code) {
@@ -155,7 +157,8 @@ __global__ void __launch_bounds__(kSpThreads, 1)
         const uint32_t p = P.p[i];
         uint32_t t = 1;
         for (int s = 0; s < (j < 7 ? j : 7); ++s) t = (t * 256u) % p;  // 2^(8 min(j,7)) mod p
-        const uint32_t c = j < 7 ? t : (t == 0 ? 0u : p - t);          // j = 7: (-2^56) mod p
+        uint32_t c = j < 7 ? t : (t == 0 ? 0u : p - t);                // j = 7: (-2^56) mod p
+        c = (c * P.mult[i]) % p;                                       // the folded factor
         const int k = g * 8 + j;
         sW[(m >> 3) * Cfg::kSbo + (k >> 4) * 128 + (m & 7) * 16 + (k & 15)] =
             static_cast<uint8_t>(c);
@@ -478,7 +481,10 @@ cudaError_t launch_split_tc(const double *X, int64_t outer, int64_t kdim, int64_
     P.bits = C.bits;
     P.n_mod = C.n_mod;
     P.err = err;
-    for (int i = 0; i < C.n_mod; ++i) P.p[i] = C.mm.p[i];
+    for (int i = 0; i < C.n_mod; ++i) {
+        P.p[i] = C.mm.p[i];
+        P.mult[i] = C.mult[i];
+    }
 #define TI_SPLIT_TC(GG, FM)                                                               \
     return rows ? launch_split_tc_t<GG, true, FM>(tm, P, num_sms, stream)                 \
                 : launch_split_tc_t<GG, false, FM>(tm, P, num_sms, stream);

@@ -2,21 +2,43 @@
 
 Same algorithm, pivot order and arithmetic as the reference (src/tensor_inv/lu.py:6-54):
 an unblocked panel with partial pivoting, a triangular solve for the U block row, and the
-trailing update ``W[jb:, jb:] -= crt_matmul(W[jb:, j:jb], W[j:jb, jb:])``.  On CUDA the
-update is fused into the CRT reconstruction (``crt_matmul_update``): identical bits, no
+trailing update ``W[jb:, jb:] -= crt_matmul(W[jb:, j:jb], W[j:jb, jb:])``.  On CUDA with
+float64 the panel is one cooperative kernel per block column (``ti_lu_panel``: the same IEEE
+operations in the same order, without the reference's two host round trips per column) and
+the update is fused into the CRT reconstruction (``crt_matmul_update``): identical bits, no
 temporary product.
 """
 
 import torch
 
-from tensor_inv_b200.crt_matmul import crt_matmul, crt_matmul_update
+from tensor_inv_b200.crt_matmul import caller_moduli, crt_matmul, crt_matmul_update
+
+
+def _panel_torch(W, piv, j, jb):
+    """The reference's unblocked panel (lu.py:24-34), op for op."""
+    for k in range(j, jb):
+        max_idx = W[k:, k].abs().argmax() + k
+        if max_idx != k:
+            W[k], W[max_idx] = W[max_idx].clone(), W[k].clone()
+            piv[k], piv[max_idx] = piv[max_idx].clone(), piv[k].clone()
+
+        if W[k, k].abs() > 1e-15:
+            W[k + 1 :, k] /= W[k, k]
+            W[k + 1 :, k + 1 : jb] -= W[k + 1 :, k : k + 1] @ W[k : k + 1, k + 1 : jb]
+
+
+# Set by tests to run the reference's torch panel loop on CUDA as well (for comparisons).
+_TORCH_PANEL = False
 
 
 def _trailing_update(W, j, jb):
-    if W.is_cuda:
-        crt_matmul_update(W[jb:, jb:], W[jb:, j:jb], W[j:jb, jb:], alpha=-1)
+    # fused into the reconstruction when W is row-major (the kernel's output layout); the
+    # same bits either way
+    mods = caller_moduli(jb - j)  # same bits as the reference's primes, fewer GEMMs
+    if W.is_cuda and W.dtype == torch.float64 and W.stride(1) == 1:
+        crt_matmul_update(W[jb:, jb:], W[jb:, j:jb], W[j:jb, jb:], alpha=-1, moduli=mods)
     else:
-        W[jb:, jb:] -= crt_matmul(W[jb:, j:jb], W[j:jb, jb:])
+        W[jb:, jb:] -= crt_matmul(W[jb:, j:jb], W[j:jb, jb:], moduli=mods)
 
 
 def lu(A, block_size=64):
@@ -29,23 +51,25 @@ def lu(A, block_size=64):
         raise ValueError(f"expected square matrix, got {A.shape}")
 
     n = A.shape[0]
-    W = A.clone()
+    device_panel = A.is_cuda and A.dtype == torch.float64 and not _TORCH_PANEL
+    # the device panel wants a row-major W; the values (and so every result bit) are the same
+    W = A.contiguous().clone() if device_panel else A.clone()
     piv = torch.arange(n, device=A.device)
+    if device_panel:
+        from tensor_inv_b200 import _native as nat
+
+        ws = torch.empty(nat.lu_panel_workspace_size(), dtype=torch.uint8, device=A.device)
+        stream = torch.cuda.current_stream(A.device)
 
     for j in range(0, n, block_size):
         b = min(block_size, n - j)
         jb = j + b
 
         # panel: unblocked LU with partial pivoting (lu.py:24-34)
-        for k in range(j, jb):
-            max_idx = W[k:, k].abs().argmax() + k
-            if max_idx != k:
-                W[k], W[max_idx] = W[max_idx].clone(), W[k].clone()
-                piv[k], piv[max_idx] = piv[max_idx].clone(), piv[k].clone()
-
-            if W[k, k].abs() > 1e-15:
-                W[k + 1 :, k] /= W[k, k]
-                W[k + 1 :, k + 1 : jb] -= W[k + 1 :, k : k + 1] @ W[k : k + 1, k + 1 : jb]
+        if device_panel and b <= 1024:
+            nat.lu_panel(W, j, jb, piv, ws, stream)
+        else:
+            _panel_torch(W, piv, j, jb)
 
         if jb < n:
             # triangular solve for the U block row (lu.py:38-43)

@@ -6,7 +6,13 @@ Same algorithm, RNG consumption and call order as the reference
 
 import torch
 
-from tensor_inv_b200.crt_matmul import crt_matmul
+from tensor_inv_b200.crt_matmul import caller_moduli, crt_matmul
+
+
+def _mm(X, Y):
+    """crt_matmul with the moduli set that keeps every bit at this inner dimension (the
+    same result as the reference's primes, fewer residue GEMMs)."""
+    return crt_matmul(X, Y, moduli=caller_moduli(X.shape[1]))
 
 
 def rsvd(A, rank, n_oversamples=10, n_power_iter=1):
@@ -22,17 +28,17 @@ def rsvd(A, rank, n_oversamples=10, n_power_iter=1):
 
     # random projection (rsvd.py:18-20)
     Omega = torch.randn(n, r, dtype=dtype, device=device)
-    Y = crt_matmul(A, Omega)
+    Y = _mm(A, Omega)
     Q, _ = torch.linalg.qr(Y)
 
     # power iterations (rsvd.py:23-25)
     for _ in range(n_power_iter):
-        Y = crt_matmul(A, crt_matmul(A.T, Q))
+        Y = _mm(A, _mm(A.T, Q))
         Q, _ = torch.linalg.qr(Y)
 
     # project to the low-rank subspace (rsvd.py:28-30)
-    B = crt_matmul(Q.T, A)
+    B = _mm(Q.T, A)
     Ub, S, Vt = torch.linalg.svd(B, full_matrices=False)
-    U = crt_matmul(Q, Ub)
+    U = _mm(Q, Ub)
 
     return U[:, :rank], S[:rank], Vt[:rank]

@@ -21,3 +21,58 @@ def test_lu(device):
 def test_lu_rejects_non_square():
     with pytest.raises(ValueError):
         lu(torch.zeros(3, 4, dtype=torch.float64))
+
+
+def _lu_both(A, block_size, monkeypatch):
+    import importlib
+
+    lu_mod = importlib.import_module("tensor_inv_b200.lu")  # the module, not the function
+
+    monkeypatch.setattr(lu_mod, "_TORCH_PANEL", True)
+    ref = lu(A, block_size=block_size)
+    monkeypatch.setattr(lu_mod, "_TORCH_PANEL", False)
+    got = lu(A, block_size=block_size)
+    return ref, got
+
+
+def _same_bits(a, b):
+    return torch.equal(a.contiguous().view(torch.int64), b.contiguous().view(torch.int64))
+
+
+def _ties(n):
+    # small integers: many equal |entries| in a column, so the argmax tie rule decides pivots
+    g = torch.Generator().manual_seed(7)
+    return torch.randint(-3, 4, (n, n), generator=g).to(torch.float64)
+
+
+def _zero_column(n):
+    g = torch.Generator().manual_seed(8)
+    A = torch.randn(n, n, generator=g, dtype=torch.float64)
+    A[:, 5] = 0.0       # a pivot below 1e-15: the reference skips that column
+    A[:, 40] = 1e-17
+    return A
+
+
+@pytest.mark.parametrize("n,block,make", [
+    (128, 32, None), (300, 64, None), (1000, 256, None), (257, 256, None),
+    (96, 32, _ties), (200, 64, _zero_column),
+])
+def test_device_panel_is_bit_identical(monkeypatch, n, block, make):
+    """The cooperative panel kernel gives exactly the reference's torch loop's P, L, U."""
+    if make is None:
+        g = torch.Generator().manual_seed(n)
+        A = torch.randn(n, n, generator=g, dtype=torch.float64)
+    else:
+        A = make(n)
+    (P0, L0, U0), (P1, L1, U1) = _lu_both(A.cuda(), block, monkeypatch)
+    assert _same_bits(P0, P1) and _same_bits(L0, L1) and _same_bits(U0, U1)
+    if make is None:
+        err = ((P1 @ A.cuda() - L1 @ U1).abs().max() / A.abs().max()).item()
+        assert err < 1e-10
+
+
+def test_device_panel_transposed_input(monkeypatch):
+    g = torch.Generator().manual_seed(11)
+    A = torch.randn(150, 150, generator=g, dtype=torch.float64).cuda().t()  # column-major view
+    (P0, L0, U0), (P1, L1, U1) = _lu_both(A, 64, monkeypatch)
+    assert _same_bits(P0, P1) and _same_bits(L0, L1) and _same_bits(U0, U1)
