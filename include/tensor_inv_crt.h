@@ -131,6 +131,13 @@ typedef struct ti_crt_options {
                                of band b overlaps the split of band b+1 and the reconstruction
                                of band b-1 (opt-in: on B200 the shared SMs slow the GEMM more
                                than the overlap saves) */
+    int lower;              /* 0: every element of C.  1: only elements C[r][c] with r >= c are
+                               guaranteed (a symmetric update such as Cholesky's
+                               W -= L21 L21^T, which reads only the lower triangle): output tiles
+                               entirely above the diagonal are skipped by the residue GEMM and
+                               the reconstruction, and those elements may or may not be written.
+                               Honoured by the single-band device path; otherwise ignored (every
+                               element is computed) */
 } ti_crt_options_t;
 
 /* The moduli count, the precision actually kept, and (if moduli_out != NULL, room for 32)

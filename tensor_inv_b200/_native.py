@@ -40,7 +40,8 @@ class CrtOptions(ctypes.Structure):
     """ti_crt_options_t."""
 
     _fields_ = [("moduli", ctypes.c_int), ("n_moduli", ctypes.c_int),
-                ("stage_events", ctypes.c_void_p * 4), ("bands", ctypes.c_int)]
+                ("stage_events", ctypes.c_void_p * 4), ("bands", ctypes.c_int),
+                ("lower", ctypes.c_int)]
 
 
 _opt = ctypes.POINTER(CrtOptions)
@@ -129,8 +130,9 @@ def crt_workspace_size(m: int, n: int, k: int, bits: int) -> int:
     return out.value
 
 
-def options(moduli=None, n_moduli=None, events=None, bands=0) -> CrtOptions:
-    """ti_crt_options_t from Python values: moduli None/'primes' or 'wide'; bands 0 = auto."""
+def options(moduli=None, n_moduli=None, events=None, bands=0, lower=False) -> CrtOptions:
+    """ti_crt_options_t from Python values: moduli None/'primes' or 'wide'; bands 0 = auto;
+    lower: only C[r][c] with r >= c is needed."""
     if moduli in (None, "primes"):
         kind = TI_MODULI_PRIMES
     elif moduli == "wide":
@@ -142,6 +144,7 @@ def options(moduli=None, n_moduli=None, events=None, bands=0) -> CrtOptions:
         raise ValueError("n_moduli must be positive")
     o = CrtOptions(kind, n)
     o.bands = int(bands)
+    o.lower = 1 if lower else 0
     if events is not None:
         for i, e in enumerate(events):
             o.stage_events[i] = e

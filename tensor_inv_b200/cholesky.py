@@ -40,7 +40,9 @@ def cholesky(A, block_size=64):
             L21 = L[jb:, j:jb]
             mods = caller_moduli(b)  # same bits as the reference's primes, fewer GEMMs
             if W.is_cuda and W.dtype == torch.float64 and W.stride(1) == 1:
-                crt_matmul_update(W[jb:, jb:], L21, L21.T, alpha=-1, moduli=mods)
+                # only W's lower triangle is read again (cholesky.py:24-30), so tiles
+                # entirely above the diagonal are skipped: the same L, half the update
+                crt_matmul_update(W[jb:, jb:], L21, L21.T, alpha=-1, moduli=mods, lower=True)
             else:
                 W[jb:, jb:] -= crt_matmul(L21, L21.T, moduli=mods)
 

@@ -247,12 +247,15 @@ def caller_moduli(k):
     return "wide" if 0 < k <= nat.TI_MAX_K_WIDE else None
 
 
-def crt_matmul_update(C, A, B, alpha=-1, *, moduli=None, n_moduli=None):
+def crt_matmul_update(C, A, B, alpha=-1, *, moduli=None, n_moduli=None, lower=False):
     """In-place ``C += alpha * crt_matmul(A, B)`` for alpha in {-1, +1}, C float64 CUDA.
 
     Bit-identical to ``C -= crt_matmul(A, B)`` (alpha=-1) or ``C += crt_matmul(A, B)``:
     the product is rounded to float64 first, then one IEEE subtraction/addition, fused
-    into the reconstruction kernel so no temporary product is materialised.
+    into the reconstruction kernel so no temporary product is materialised.  ``lower=True``
+    guarantees only the elements C[r, c] with r >= c (the others may be left unchanged):
+    output tiles entirely above the diagonal are skipped, about half the work of a
+    symmetric update.
     """
     bits = _check_dtype(A)
     if alpha not in (-1, 1):
@@ -265,6 +268,7 @@ def crt_matmul_update(C, A, B, alpha=-1, *, moduli=None, n_moduli=None):
     if m == 0 or B.shape[1] == 0 or k == 0:
         return C
     opt = _options(k, bits, moduli, n_moduli)
+    opt.lower = 1 if lower else 0
     A = A.to(device=C.device, dtype=torch.float64)
     B = B.to(device=C.device, dtype=torch.float64)
     return _launch_crt_matmul(A, B, C, bits,

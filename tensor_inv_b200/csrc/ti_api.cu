@@ -20,11 +20,11 @@ cudaError_t launch_residue_gemm(const int8_t *a_res, const int8_t *b_res, int64_
                                 void *out, int64_t ldo, int out_i32, int *err, int num_sms,
                                 cudaStream_t stream, int64_t a_plane = 0, int64_t b_plane = 0,
                                 int64_t out_plane = 0, const uint32_t *weights = nullptr,
-                                bool unsigned_ops = false);
+                                bool unsigned_ops = false, bool lower = false);
 cudaError_t launch_crt(const void *R, bool in_u8, int64_t ldr, int64_t plane, int64_t rows,
                        int64_t cols, const int32_t *row_exp, const int32_t *col_exp, double *C,
                        int64_t ldc, int out_mode, const CrtConst &K, int num_sms,
-                       cudaStream_t stream, int blocks_per_sm = 8);
+                       cudaStream_t stream, int blocks_per_sm = 8, bool lower = false);
 cudaError_t launch_split_tc(const double *X, int64_t outer, int64_t kdim, int64_t s_outer,
                             int64_t s_k, const SplitConst &C, const int32_t *exps, int8_t *res,
                             int64_t ld_res, int64_t plane, int *err, int num_sms,
@@ -32,7 +32,7 @@ cudaError_t launch_split_tc(const double *X, int64_t outer, int64_t kdim, int64_
 cudaError_t launch_crt_tc(const uint8_t *R, int64_t ldr, int64_t plane, int64_t rows,
                           int64_t cols, const int32_t *row_exp, const int32_t *col_exp, double *C,
                           int64_t ldc, int out_mode, const CrtConst &K, int *err, int num_sms,
-                          cudaStream_t stream);
+                          cudaStream_t stream, bool lower);
 int64_t gemm_output_tiles(int64_t m, int64_t n);
 size_t fused_scratch_bytes(int n_mod, int num_ctas);
 cudaError_t launch_fused_gemm_crt(const int8_t *a_res, const int8_t *b_res, int64_t m, int64_t n,
@@ -64,14 +64,15 @@ static bool use_fused(int64_t m, int64_t n) {
 static cudaError_t launch_k3(const uint8_t *R, int64_t ldr, int64_t plane, int64_t rows,
                              int64_t cols, const int32_t *rexp, const int32_t *cexp, double *C,
                              int64_t ldc, int out_mode, const CrtConst &K, int *err, int sms,
-                             cudaStream_t s, int blocks_per_sm = 8) {
+                             cudaStream_t s, int blocks_per_sm = 8, bool lower = false) {
     const char *e = getenv("TI_CRT_K3");
     if (e && !strcmp(e, "simt"))
         return launch_crt(R, true, ldr, plane, rows, cols, rexp, cexp, C, ldc, out_mode, K, sms,
-                          s, blocks_per_sm);
+                          s, blocks_per_sm, lower);
     int ctas = sms * blocks_per_sm / 8;
     if (ctas < 1) ctas = 1;
-    return launch_crt_tc(R, ldr, plane, rows, cols, rexp, cexp, C, ldc, out_mode, K, err, ctas, s);
+    return launch_crt_tc(R, ldr, plane, rows, cols, rexp, cexp, C, ldc, out_mode, K, err, ctas, s,
+                         lower);
 }
 
 // The device error word: kernels record a bounded wait that ran out here.
@@ -777,12 +778,14 @@ int ti_crt_matmul_ex(const double *A, int64_t sa0, int64_t sa1, const double *B,
         return TI_OK;
     }
     // K2: per-modulus residue GEMMs, mod-reduced to uint8 planes
+    const bool lower = opt && opt->lower;
     e = launch_residue_gemm(ares, bres, m, n, k, L.ldk, L.n_mod, SC.mm, R, L.ldr, 0, d.err,
-                            d.num_sms, s, 0, 0, 0, nullptr, !SC.symmetric);
+                            d.num_sms, s, 0, 0, 0, nullptr, !SC.symmetric, lower);
     if (e != cudaSuccess) return e == cudaErrorInvalidValue ? TI_ERR_NO_DEVICE : TI_ERR_CUDA;
     // K3: exact CRT + inverse scaling
     record(ev, 2, s);
-    e = launch_k3(R, L.ldr, m * L.ldr, m, n, rexp, cexp, C, ldc, out_mode, KC, d.err, d.num_sms, s);
+    e = launch_k3(R, L.ldr, m * L.ldr, m, n, rexp, cexp, C, ldc, out_mode, KC, d.err, d.num_sms, s,
+                  8, lower);
     record(ev, 3, s);
     return cuda_status(e);
 }

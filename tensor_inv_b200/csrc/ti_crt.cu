@@ -35,7 +35,7 @@ template <bool kInU8, int kOutMode, int kMaxM>
 __global__ void __launch_bounds__(256, 3) crt_kernel(
     const void *__restrict__ Rv, int64_t ldr, int64_t plane, int64_t rows, int64_t cols,
     const int32_t *__restrict__ row_exp, const int32_t *__restrict__ col_exp,
-    double *__restrict__ C, int64_t ldc, const __grid_constant__ CrtConst K) {
+    double *__restrict__ C, int64_t ldc, int lower, const __grid_constant__ CrtConst K) {
     const int64_t groups = (cols + 3) >> 2;
     const bool vec_out = ((reinterpret_cast<uintptr_t>(C) & 15) == 0) && ((ldc & 1) == 0);
     for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
@@ -43,6 +43,7 @@ __global__ void __launch_bounds__(256, 3) crt_kernel(
         for (int64_t g = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < groups;
              g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
             const int64_t col = g << 2;
+            if (lower && col > row) continue;  // the group lies above the diagonal
             const int nc = cols - col < 4 ? static_cast<int>(cols - col) : 4;
             // t bytes of every modulus, 4 columns per word, all loads in flight at once
             uint32_t w[kMaxM];
@@ -118,7 +119,7 @@ template <bool kInU8>
 static cudaError_t launch_crt_t(const void *R, int64_t ldr, int64_t plane, int64_t rows,
                                 int64_t cols, const int32_t *row_exp, const int32_t *col_exp,
                                 double *C, int64_t ldc, int out_mode, const CrtConst &K,
-                                int num_sms, cudaStream_t stream, int blocks_per_sm) {
+                                int num_sms, cudaStream_t stream, int blocks_per_sm, int lower) {
     const int64_t groups = (cols + 3) >> 2;
     int64_t gx = (groups + 255) / 256;
     int64_t cap = int64_t(num_sms) * blocks_per_sm;
@@ -132,10 +133,11 @@ static cudaError_t launch_crt_t(const void *R, int64_t ldr, int64_t plane, int64
 #define TI_CRT_LAUNCH(MODE)                                                                      \
     if (small)                                                                                   \
         crt_kernel<kInU8, MODE, 16><<<g, 256, 0, stream>>>(R, ldr, plane, rows, cols, row_exp,  \
-                                                           col_exp, C, ldc, K);                  \
+                                                           col_exp, C, ldc, lower, K);           \
     else                                                                                         \
         crt_kernel<kInU8, MODE, kMaxModuli><<<g, 256, 0, stream>>>(R, ldr, plane, rows, cols,   \
-                                                                   row_exp, col_exp, C, ldc, K);
+                                                                   row_exp, col_exp, C, ldc,    \
+                                                                   lower, K);
     if (out_mode == 0) {
         TI_CRT_LAUNCH(0)
     } else if (out_mode == 1) {
@@ -150,13 +152,13 @@ static cudaError_t launch_crt_t(const void *R, int64_t ldr, int64_t plane, int64
 cudaError_t launch_crt(const void *R, bool in_u8, int64_t ldr, int64_t plane, int64_t rows,
                        int64_t cols, const int32_t *row_exp, const int32_t *col_exp, double *C,
                        int64_t ldc, int out_mode, const CrtConst &K, int num_sms,
-                       cudaStream_t stream, int blocks_per_sm) {
+                       cudaStream_t stream, int blocks_per_sm, bool lower) {
     if (rows == 0 || cols == 0) return cudaSuccess;
     if (in_u8)
         return launch_crt_t<true>(R, ldr, plane, rows, cols, row_exp, col_exp, C, ldc, out_mode, K,
-                                  num_sms, stream, blocks_per_sm);
+                                  num_sms, stream, blocks_per_sm, lower ? 1 : 0);
     return launch_crt_t<false>(R, ldr, plane, rows, cols, row_exp, col_exp, C, ldc, out_mode, K,
-                               num_sms, stream, blocks_per_sm);
+                               num_sms, stream, blocks_per_sm, lower ? 1 : 0);
 }
 
 }  // namespace ti

@@ -61,9 +61,15 @@ struct CrtTcParams {
     double *C;
     int64_t ldc;
     int out_mode;  // 0 store, 1 subtract, 2 add
+    int lower;     // skip units entirely above the diagonal
     int *err;
     CrtConst K;
 };
+
+// A unit (4 rows x 128 columns) lies entirely above the diagonal: all roles skip it.
+__device__ __forceinline__ bool tc_skip(const CrtTcParams &P, int64_t rb, int64_t cb) {
+    return P.lower && cb * kTcCols > rb * kTcRows + (kTcRows - 1);
+}
 
 __device__ __forceinline__ void tc_raise(const CrtTcParams &P, volatile int *abort, int code) {
     *abort = 1;
@@ -232,6 +238,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
             uint32_t phase = 0, issued_mask = 0, issued_phase = 0;
             bool ok = true;
             for (GridIter it(P.col_blocks); it.a < P.row_blocks; it.next()) {
+                if (tc_skip(P, it.a, it.b)) continue;
                 const int64_t cb = it.b, r0 = it.a * kTcRows;
                 const int nr = P.rows - r0 < kTcRows ? static_cast<int>(P.rows - r0) : kTcRows;
                 if (!mbar_wait(&empty[stage], phase ^ 1, abort)) {
@@ -264,9 +271,11 @@ __global__ void __launch_bounds__(kTcThreads, 2)
             uint32_t phase = 0;
             bool ok = true, any_issued = false;
             int64_t local = 0;
-            for (GridIter it(P.col_blocks); it.a < P.row_blocks; it.next(), ++local) {
+            for (GridIter it(P.col_blocks); it.a < P.row_blocks; it.next()) {
+                if (tc_skip(P, it.a, it.b)) continue;
                 const int acc = static_cast<int>(local % kTcAcc);
                 const uint32_t acc_phase = static_cast<uint32_t>((local / kTcAcc) & 1);
+                ++local;
                 if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort) ||
                     !mbar_wait(&full[stage], phase, abort)) {
                     tc_raise(P, abort, kErrTimeoutMma);
@@ -300,9 +309,11 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         const int m = q * 32 + lane;    // column within the unit (TMEM lane)
         const CrtConst &K = P.K;
         int64_t local = 0;
-        for (GridIter it(P.col_blocks); it.a < P.row_blocks; it.next(), ++local) {
+        for (GridIter it(P.col_blocks); it.a < P.row_blocks; it.next()) {
+            if (tc_skip(P, it.a, it.b)) continue;
             const int acc = static_cast<int>(local % kTcAcc);
             const uint32_t acc_phase = static_cast<uint32_t>((local / kTcAcc) & 1);
+            ++local;
             if (!mbar_wait(&tfull[acc], acc_phase, abort)) {
                 tc_raise(P, abort, kErrTimeoutEpilogue);
                 break;
@@ -350,7 +361,7 @@ static cudaError_t configure_tc(int dev) {
 cudaError_t launch_crt_tc(const uint8_t *R, int64_t ldr, int64_t plane, int64_t rows,
                           int64_t cols, const int32_t *row_exp, const int32_t *col_exp, double *C,
                           int64_t ldc, int out_mode, const CrtConst &K, int *err, int num_sms,
-                          cudaStream_t stream) {
+                          cudaStream_t stream, bool lower) {
     if (rows == 0 || cols == 0) return cudaSuccess;
     if ((reinterpret_cast<uintptr_t>(R) & 15) || (ldr & 15) || (plane & 15) || K.n_mod > kTcK)
         return cudaErrorInvalidValue;
@@ -382,6 +393,7 @@ cudaError_t launch_crt_tc(const uint8_t *R, int64_t ldr, int64_t plane, int64_t 
     P.C = C;
     P.ldc = ldc;
     P.out_mode = out_mode;
+    P.lower = lower ? 1 : 0;
     P.err = err;
     P.K = K;
     const int64_t grid = units < 2 * int64_t(num_sms) ? units : 2 * int64_t(num_sms);

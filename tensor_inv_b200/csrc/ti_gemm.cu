@@ -57,6 +57,7 @@ struct GemmParams {
     int out_i32;       // 0: uint8 residues (|accumulator| <= 2^31 - 256); 1: int32, any int8
     int store_t;       // uint8 output holds t = (r * crt.u[i]) mod p instead of r
     uint32_t idesc;    // MMA instruction descriptor: signed or unsigned 8-bit operands
+    int lower;         // unfused: skip output tiles entirely above the diagonal
     // fused output
     uint8_t *scratch;  // 2 slots x n_mod x 128 x 256 bytes per CTA
     const int32_t *row_exp, *col_exp;
@@ -89,6 +90,8 @@ __device__ __forceinline__ void for_each_unit(const GemmParams &P, F &&f) {
             const int mod = static_cast<int>(u / per_mod);
             int tm, tn;
             decode_tile(P, u - int64_t(mod) * per_mod, tm, tn);
+            // every role skips the same tiles (first column past the last row)
+            if (P.lower && int64_t(tn) * kBN > int64_t(tm) * kBM + (kBM - 1)) continue;
             if (!f(mod, tm, tn, int64_t(0))) return;
         }
     } else {
@@ -529,12 +532,13 @@ int gemm_smem_bytes() { return static_cast<int>(kGemmSmemBytes); }
 // pass their full operands' strides.
 // weights: if not null, the uint8 output holds t_i = (r_i * weights[i]) mod p_i.
 // unsigned_ops: the residue planes hold unsigned bytes (floor-mod residues up to 254)
-// instead of signed ones.
+// instead of signed ones.  lower: output tiles entirely above the diagonal are skipped.
 cudaError_t launch_residue_gemm(const int8_t *a_res, const int8_t *b_res, int64_t m, int64_t n,
                                 int64_t kdim, int64_t ld, int n_mod, const ModMagic &mm,
                                 void *out, int64_t ldo, int out_i32, int *err, int num_sms,
                                 cudaStream_t stream, int64_t a_plane, int64_t b_plane,
-                                int64_t out_plane, const uint32_t *weights, bool unsigned_ops) {
+                                int64_t out_plane, const uint32_t *weights, bool unsigned_ops,
+                                bool lower) {
     if (m == 0 || n == 0 || n_mod == 0) return cudaSuccess;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -549,6 +553,7 @@ cudaError_t launch_residue_gemm(const int8_t *a_res, const int8_t *b_res, int64_
     P.ldo = ldo;
     P.plane = out_plane ? out_plane : m * ldo;
     P.out_i32 = out_i32;
+    P.lower = lower ? 1 : 0;
     if (weights && !out_i32) {
         P.store_t = 1;
         for (int i = 0; i < n_mod; ++i) P.crt.u[i] = weights[i];

@@ -593,3 +593,21 @@ def test_host_result_blocks_are_reused(ti):
         C = ti.crt_matmul(A, B)   # the previous result dies when C is rebound
         ptrs.add(C.data_ptr())
     assert len(ptrs) <= 2
+
+
+# ---------------------------------------------------------------------------------------
+# lower-triangle updates (symmetric trailing updates)
+# ---------------------------------------------------------------------------------------
+@pytest.mark.parametrize("n,k,k3", [(300, 256, "tc"), (1030, 129, "tc"), (517, 64, "simt"),
+                                    (2000, 256, "tc")])
+def test_lower_update_matches_full_on_lower_triangle(ti, monkeypatch, n, k, k3):
+    if k3 == "simt":
+        monkeypatch.setenv("TI_CRT_K3", "simt")
+    L21 = _rand((n, k), 7100 + n, 1.0).cuda()
+    W0 = _rand((n, n), 7200 + n).cuda()
+    full = W0.clone()
+    ti.crt_matmul_update(full, L21, L21.T, alpha=-1, moduli="wide")
+    low = W0.clone()
+    ti.crt_matmul_update(low, L21, L21.T, alpha=-1, moduli="wide", lower=True)
+    mask = torch.ones(n, n, dtype=torch.bool, device="cuda").tril()
+    assert torch.equal(full[mask].view(torch.int64), low[mask].view(torch.int64))
