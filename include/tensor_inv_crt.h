@@ -106,6 +106,27 @@ int ti_crt_reconstruct(const int32_t *residues, const int32_t *moduli, int n_mod
                        const int32_t *row_exp, const int32_t *col_exp, int64_t rows,
                        int64_t cols, double *out, int64_t ldo, void *stream);
 
+/*
+ * One rank's share of a product whose inner dimension is split across ranks, C = sum_r A_r B_r
+ * (the contractions over the row-sharded dimension of a distributed rSVD, A^T Q and Q^T A).
+ * With the exponents of the whole product given (row_exp: frexp exponents of max |A[i, :]|
+ * over every rank's columns, col_exp likewise for B's columns; TI_NONFINITE_EXP for a
+ * non-finite row/column), writes this rank's residue products (A_r B_r) mod p_i as int32 planes
+ * out[i][m][n] in [0, p_i), for the first n_mod primes (n_mod = ti_n_moduli of the WHOLE inner
+ * dimension).  The element-wise sum of all ranks' planes (an int32 all-reduce; below
+ * ranks * 127) passed to ti_crt_reconstruct with the same exponents and moduli gives the
+ * crt_matmul of the whole product bit for bit.  A: m x k (this rank's k), B: k x n, strides
+ * in elements with one of each pair 1.  No counterpart in the reference, which runs on one
+ * device; it splits crt_matmul.py:101-126 at _matmul_residues.
+ * workspace: ti_crt_residue_partial_workspace_size() bytes, 256-byte aligned.
+ */
+int ti_crt_residue_partial_workspace_size(int64_t m, int64_t n, int64_t k, int n_mod,
+                                          size_t *bytes);
+int ti_crt_residue_partial(const double *A, int64_t sa0, int64_t sa1, const double *B,
+                           int64_t sb0, int64_t sb1, int64_t m, int64_t n, int64_t k, int bits,
+                           int n_mod, const int32_t *row_exp, const int32_t *col_exp,
+                           int32_t *out, void *workspace, size_t workspace_bytes, void *stream);
+
 /* Moduli sets.  TI_MODULI_PRIMES is the reference's (the first N odd primes, 3..127,
    N from _n_moduli).  TI_MODULI_WIDE is an opt-in extension:
    pairwise-coprime odd moduli up to 255 (255, 253, 251, 247, 241, 239, 233, 229, 227, 223,

@@ -70,6 +70,10 @@ SIGNATURES = {
     "ti_crt_matmul_host": (_int, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i64, _i64,
                                   _int, _p, _sz, _p, _opt]),
     "ti_device_error": (_int, [ctypes.POINTER(_int), _int]),
+    "ti_crt_residue_partial_workspace_size": (_int, [_i64, _i64, _i64, _int,
+                                                     ctypes.POINTER(_sz)]),
+    "ti_crt_residue_partial": (_int, [_p, _i64, _i64, _p, _i64, _i64, _i64, _i64, _i64, _int,
+                                      _int, _p, _p, _p, _p, _sz, _p]),
     "ti_lu_panel_workspace_size": (_int, [ctypes.POINTER(_sz)]),
     "ti_lu_panel": (_int, [_p, _i64, _i64, _i64, _i64, _p, _p, _sz, _p]),
 }

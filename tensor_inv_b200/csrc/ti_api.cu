@@ -14,7 +14,7 @@ namespace ti {
 cudaError_t launch_split(const double *X, int64_t outer, int64_t kdim, int64_t s_outer,
                          int64_t s_k, const SplitConst &C, int32_t *exp_out, int8_t *res,
                          int64_t ld_res, int num_sms, cudaStream_t stream, int64_t plane = 0,
-                         int blocks_per_sm = 8, int *err = nullptr);
+                         int blocks_per_sm = 8, int *err = nullptr, bool exps_given = false);
 cudaError_t launch_residue_gemm(const int8_t *a_res, const int8_t *b_res, int64_t m, int64_t n,
                                 int64_t kdim, int64_t ld, int n_mod, const ModMagic &mm,
                                 void *out, int64_t ldo, int out_i32, int *err, int num_sms,
@@ -541,6 +541,55 @@ int ti_crt_split(const double *X, int64_t outer, int64_t kdim, int64_t s_outer, 
     const int64_t so = (s_k == 1) ? s_outer : 1;
     return cuda_status(launch_split(X, outer, kdim, so, sk, C, exp_out, res_out, ld_res,
                                     d.num_sms, static_cast<cudaStream_t>(stream)));
+}
+
+int ti_crt_residue_partial_workspace_size(int64_t m, int64_t n, int64_t k, int n_mod,
+                                          size_t *bytes) {
+    if (!bytes || m < 0 || n < 0 || k < 0 || n_mod < 1 || n_mod > 30)
+        return TI_ERR_INVALID_ARGUMENT;
+    const int64_t ldk = round_up(k > 0 ? k : 1, 16);
+    *bytes = align256(size_t(n_mod) * size_t(m) * size_t(ldk)) +
+             align256(size_t(n_mod) * size_t(n) * size_t(ldk));
+    return TI_OK;
+}
+
+int ti_crt_residue_partial(const double *A, int64_t sa0, int64_t sa1, const double *B,
+                           int64_t sb0, int64_t sb1, int64_t m, int64_t n, int64_t k, int bits,
+                           int n_mod, const int32_t *row_exp, const int32_t *col_exp,
+                           int32_t *out, void *workspace, size_t workspace_bytes, void *stream) {
+    if (m < 0 || n < 0 || k < 0 || n_mod < 1 || n_mod > 30) return TI_ERR_INVALID_ARGUMENT;
+    if (bits < 1 || bits > 53) return TI_ERR_INVALID_ARGUMENT;
+    if (k > int64_t(TI_MAX_K)) return TI_ERR_UNSUPPORTED;
+    if (m == 0 || n == 0) return TI_OK;
+    if (!out || !row_exp || !col_exp) return TI_ERR_INVALID_ARGUMENT;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (k == 0)  // an empty slice contributes zero residues
+        return cuda_status(cudaMemsetAsync(out, 0, sizeof(int32_t) * n_mod * m * n, s));
+    if (!A || !B) return TI_ERR_INVALID_ARGUMENT;
+    if (!(sa1 == 1 || sa0 == 1) || !(sb0 == 1 || sb1 == 1)) return TI_ERR_INVALID_ARGUMENT;
+    size_t need = 0;
+    ti_crt_residue_partial_workspace_size(m, n, k, n_mod, &need);
+    if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255))
+        return TI_ERR_WORKSPACE;
+    DevInfo d;
+    int rc = device_info(d);
+    if (rc != TI_OK) return rc;
+    SplitConst SC;  // the reference's floor-mod residues of the first n_mod primes
+    if (!make_split_const(kPrimes, n_mod, bits, false, nullptr, SC)) return TI_ERR_INVALID_ARGUMENT;
+    const int64_t ldk = round_up(k, 16);
+    int8_t *ares = static_cast<int8_t *>(workspace);
+    int8_t *bres = ares + align256(size_t(n_mod) * size_t(m) * size_t(ldk));
+    int32_t *rexp = const_cast<int32_t *>(row_exp), *cexp = const_cast<int32_t *>(col_exp);
+    cudaError_t e;
+    if (sa1 == 1) e = launch_split(A, m, k, sa0, 1, SC, rexp, ares, ldk, d.num_sms, s, 0, 8, d.err, true);
+    else e = launch_split(A, m, k, 1, sa1, SC, rexp, ares, ldk, d.num_sms, s, 0, 8, d.err, true);
+    if (e != cudaSuccess) return TI_ERR_CUDA;
+    if (sb0 == 1) e = launch_split(B, n, k, sb1, 1, SC, cexp, bres, ldk, d.num_sms, s, 0, 8, d.err, true);
+    else e = launch_split(B, n, k, 1, sb0, SC, cexp, bres, ldk, d.num_sms, s, 0, 8, d.err, true);
+    if (e != cudaSuccess) return TI_ERR_CUDA;
+    e = launch_residue_gemm(ares, bres, m, n, k, ldk, n_mod, SC.mm, out, n, 1, d.err, d.num_sms, s);
+    if (e != cudaSuccess) return e == cudaErrorInvalidValue ? TI_ERR_NO_DEVICE : TI_ERR_CUDA;
+    return TI_OK;
 }
 
 int ti_batched_gemm_workspace_size(int64_t batch, int64_t M, int64_t K, int64_t N,

@@ -263,11 +263,13 @@ static int split_mode() {  // 0 simt, 1 tensor cores with fallback, 2 tensor cor
 
 // plane: bytes between the residue planes of consecutive moduli (0: outer * ld_res, the
 // operand's own planes; a row band of a larger operand passes the full operand's stride).
+// exps_given: exp_out already holds the exponents (for example reduced over the inner
+// dimension of several ranks), so they are read, not computed.
 // blocks_per_sm caps the grid so the kernel can share SMs with a concurrent GEMM.
 cudaError_t launch_split(const double *X, int64_t outer, int64_t kdim, int64_t s_outer,
                          int64_t s_k, const SplitConst &C, int32_t *exp_out, int8_t *res,
                          int64_t ld_res, int num_sms, cudaStream_t stream, int64_t plane,
-                         int blocks_per_sm, int *err) {
+                         int blocks_per_sm, int *err, bool exps_given) {
     if (outer == 0) return cudaSuccess;
     if (plane == 0) plane = outer * ld_res;
     const int64_t cap = int64_t(num_sms) * blocks_per_sm;
@@ -279,8 +281,9 @@ cudaError_t launch_split(const double *X, int64_t outer, int64_t kdim, int64_t s
         const int64_t warps_needed = outer;
         int64_t blocks = (warps_needed + 7) / 8;
         if (blocks > int64_t(num_sms) * 16) blocks = int64_t(num_sms) * 16;
-        exp_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(X, outer, kdim,
-                                                                           s_outer, exp_out);
+        if (!exps_given)
+            exp_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(X, outer, kdim,
+                                                                               s_outer, exp_out);
         if (try_tc) {
             const cudaError_t e = launch_split_tc(X, outer, kdim, s_outer, 1, C, exp_out, res,
                                                   ld_res, plane, err, tc_ctas, stream);
@@ -302,8 +305,9 @@ cudaError_t launch_split(const double *X, int64_t outer, int64_t kdim, int64_t s
                                                                res, ld_res, plane, C);
     } else {
         const int64_t blocks = (outer + 31) / 32;
-        exp_cols_kernel<<<static_cast<unsigned>(blocks), 1024, 0, stream>>>(X, outer, kdim, s_k,
-                                                                            exp_out);
+        if (!exps_given)
+            exp_cols_kernel<<<static_cast<unsigned>(blocks), 1024, 0, stream>>>(X, outer, kdim,
+                                                                                s_k, exp_out);
         if (try_tc) {
             const cudaError_t e = launch_split_tc(X, outer, kdim, 1, s_k, C, exp_out, res,
                                                   ld_res, plane, err, tc_ctas, stream);
