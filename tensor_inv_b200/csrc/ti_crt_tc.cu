@@ -167,9 +167,16 @@ __device__ __forceinline__ double crt_from_byte_sums(const uint32_t (&D)[32], in
     const uint64_t T = (static_cast<uint64_t>(th) << 32) | tl | (dropped != 0u ? 1u : 0u);
     double d = __ull2double_rn(T);
     if (neg) d = -d;
-    return scale_pow2_rne(d, (c3 ? 64 : 32) - static_cast<int>(sh) + e2);
+    const int sc = (c3 ? 64 : 32) - static_cast<int>(sh) + e2;
+    // Fast path: with a nonzero top limb T's leading one is bit 63, so d's biased exponent is
+    // 1086 (1087 if the rounding carried); if 1086 + sc stays within [2, 2045] the scaled value
+    // is normal and exact, and adding sc to the exponent field is the whole ldexp.
+    if (top != 0u && sc >= 2 - 1086 && sc <= 2045 - 1086)
+        return __longlong_as_double(__double_as_longlong(d) + (static_cast<long long>(sc) << 52));
+    return scale_pow2_rne(d, sc);
 }
 
+template <int kOutMode>  // 0 store, 1 subtract, 2 add
 __global__ void __launch_bounds__(kTcThreads, 2)
     crt_tc_kernel(const __grid_constant__ CUtensorMap tmT, const __grid_constant__ CrtTcParams P) {
     extern __shared__ uint8_t smem_raw[];
@@ -332,7 +339,10 @@ __global__ void __launch_bounds__(kTcThreads, 2)
             const double v = (re == kNonfiniteExp || ce == kNonfiniteExp)
                                  ? nan_value()
                                  : crt_from_byte_sums(D, re + ce - K.two_bits, K);
-            write_mode(P.C + row * P.ldc + col, v, P.out_mode);
+            double *dst = P.C + row * P.ldc + col;
+            if (kOutMode == 0) *dst = v;
+            else if (kOutMode == 1) *dst = __dsub_rn(*dst, v);
+            else *dst = __dadd_rn(*dst, v);
         }
     }
 
@@ -348,11 +358,13 @@ __global__ void __launch_bounds__(kTcThreads, 2)
 static cudaError_t configure_tc(int dev) {
     static std::atomic<int> configured{-1};  // last device configured
     if (configured.load() == dev) return cudaSuccess;
-    const cudaError_t e = cudaFuncSetAttribute(crt_tc_kernel,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(kTcSmemBytes));
-    if (e == cudaSuccess) configured.store(dev);
-    return e;
+    for (auto fn : {crt_tc_kernel<0>, crt_tc_kernel<1>, crt_tc_kernel<2>}) {
+        const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   static_cast<int>(kTcSmemBytes));
+        if (e != cudaSuccess) return e;
+    }
+    configured.store(dev);
+    return cudaSuccess;
 }
 
 // C (op)= CRT of the uint8 t-planes R[i][row][ldr] (plane bytes apart), rows x cols outputs.
@@ -397,7 +409,10 @@ cudaError_t launch_crt_tc(const uint8_t *R, int64_t ldr, int64_t plane, int64_t 
     P.err = err;
     P.K = K;
     const int64_t grid = units < 2 * int64_t(num_sms) ? units : 2 * int64_t(num_sms);
-    crt_tc_kernel<<<static_cast<unsigned>(grid), kTcThreads, kTcSmemBytes, stream>>>(tm, P);
+    const dim3 g(static_cast<unsigned>(grid));
+    if (out_mode == 0) crt_tc_kernel<0><<<g, kTcThreads, kTcSmemBytes, stream>>>(tm, P);
+    else if (out_mode == 1) crt_tc_kernel<1><<<g, kTcThreads, kTcSmemBytes, stream>>>(tm, P);
+    else crt_tc_kernel<2><<<g, kTcThreads, kTcSmemBytes, stream>>>(tm, P);
     return cudaGetLastError();
 }
 

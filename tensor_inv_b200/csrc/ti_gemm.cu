@@ -12,8 +12,12 @@
 //   warp 1      TMEM allocator + single-thread tcgen05.mma.kind::i8 issuer, M=128 N=256
 //               K=32 per instruction, int32 accumulators in TMEM, double-buffered
 //               (2 x 256 columns = all 512 TMEM columns).
-//   warps 2..5  epilogue: tcgen05.ld 32 rows x 32 columns at a time, exact mod p, pack.
-//   warps 6..9  (fused mode only) CRT: exact reconstruction of a finished output tile.
+//   warps 2..9  epilogue: tcgen05.ld 32 rows x 32 columns at a time, exact mod p, pack.  With
+//               a short K loop (k <= 512, e.g. the trailing updates of LU and Cholesky) the
+//               epilogue and not the MMA bounds a tile, so all 8 warps work, two per TMEM lane
+//               quadrant with 128 columns each; otherwise warps 2..5 take whole tile rows and
+//               warps 6..9 idle (fewer warps polling beside the MMA issuer).
+//   warps 10..13 (fused mode only) CRT: exact reconstruction of a finished output tile.
 //
 // Unfused mode: work units are (modulus, tile) in modulus-major order; the epilogue writes
 // uint8 residue planes R[i][m][ldo] (or int32 planes) that K3 (ti_crt.cu) consumes.
@@ -33,7 +37,8 @@ namespace ti {
 
 constexpr int kBM = 128, kBN = 256, kBK = 128, kStages = 4;
 constexpr int kABytes = kBM * kBK, kBBytes = kBN * kBK, kStageBytes = kABytes + kBBytes;
-constexpr int kEpiThreads = 128, kCrtThreads = 128;
+constexpr int kEpiThreads = 256, kCrtThreads = 128;
+constexpr int kEpiWarpEnd = 2 + kEpiThreads / 32;  // epilogue warps are 2 .. kEpiWarpEnd-1
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kIdesc = make_idesc_i8(kBM, kBN);
 constexpr int kGroupM = 16;  // tile raster: 16 row-tiles per group for L2 reuse
@@ -58,6 +63,7 @@ struct GemmParams {
     int store_t;       // uint8 output holds t = (r * crt.u[i]) mod p instead of r
     uint32_t idesc;    // MMA instruction descriptor: signed or unsigned 8-bit operands
     int lower;         // unfused: skip output tiles entirely above the diagonal
+    int epi_warps;     // 8 when the K loop is short (the epilogue bounds the tile), else 4
     // fused output
     uint8_t *scratch;  // 2 slots x n_mod x 128 x 256 bytes per CTA
     const int32_t *row_exp, *col_exp;
@@ -201,8 +207,8 @@ __global__ void __launch_bounds__(gemm_threads(kFused), 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], kEpiThreads);
-            mbar_init(&sfull[a], kEpiThreads);
+            mbar_init(&tempty[a], 32 * P.epi_warps);
+            mbar_init(&sfull[a], 32 * P.epi_warps);
             mbar_init(&sempty[a], kCrtThreads);
         }
         mbar_init(drain, 1);
@@ -316,10 +322,13 @@ __global__ void __launch_bounds__(gemm_threads(kFused), 1)
                 }
             }
         }
-    } else if (warp < 6) {
-        // ---------------- epilogue (warps 2..5) ----------------
+    } else if (warp < 2 + P.epi_warps) {
+        // ---------------- epilogue (warps 2..9) ----------------
         const int q = warp & 3;  // TMEM lane quadrant this warp may access
         const int row_in_tile = q * 32 + lane;
+        // 8 warps: two per quadrant, 4 column chunks each; 4 warps: all 8 chunks
+        const int c_count = P.epi_warps == 8 ? kBN / 64 : kBN / 32;
+        const int c_begin = ((warp - 2) >> 2) * c_count;
         int64_t unit = 0;
         for_each_unit<kFused>(P, [&](int mod, int tm, int tn, int64_t tile_local) {
             const int acc = static_cast<int>(unit & 1);
@@ -349,7 +358,7 @@ __global__ void __launch_bounds__(gemm_threads(kFused), 1)
                              int64_t(mod) * kSlotPlaneBytes + int64_t(row_in_tile) * kBN
                        : nullptr;
 #pragma unroll 1
-            for (int c = 0; c < kBN / 32; ++c) {
+            for (int c = c_begin; c < c_begin + c_count; ++c) {
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(tbase + c * 32, v);
                 tmem_wait_ld();
@@ -421,9 +430,9 @@ __global__ void __launch_bounds__(gemm_threads(kFused), 1)
             }
             return true;
         });
-    } else if (kFused) {
-        // ---------------- CRT warps (6..9, fused mode) ----------------
-        const int ct = threadIdx.x - 192;
+    } else if (kFused && warp >= kEpiWarpEnd) {
+        // ---------------- CRT warps (10..13, fused mode) ----------------
+        const int ct = threadIdx.x - (64 + kEpiThreads);
         const int64_t tiles = int64_t(P.tiles_m) * P.tiles_n;
         int64_t local = 0;
         for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
@@ -511,6 +520,7 @@ static cudaError_t fill_common(GemmParams &P, CUtensorMap &tmA, CUtensorMap &tmB
     P.m = m;
     P.n = n;
     P.num_kb = static_cast<int>((kdim + kBK - 1) / kBK);
+    P.epi_warps = P.num_kb <= 4 ? 8 : 4;
     P.n_mod = n_mod;
     P.tiles_m = static_cast<int>((m + kBM - 1) / kBM);
     P.tiles_n = static_cast<int>((n + kBN - 1) / kBN);
