@@ -42,6 +42,11 @@ def _worker(rank, world, port, case):
             got = D.crt_matmul_sharded_k(A[:, k0:k1].cuda(), B[k0:k1].cuda())
             want = ti.crt_matmul(A.cuda(), B.cuda())
             assert _same(got, want), "sharded-k product differs"
+            # an empty slice on one rank (all of k on the other)
+            A_e = A[:, :0] if rank == 0 else A
+            B_e = B[:0] if rank == 0 else B
+            got_e = D.crt_matmul_sharded_k(A_e.cuda(), B_e.cuda())
+            assert _same(got_e, want), "sharded-k product with an empty slice differs"
             # a transposed view on the left (the rSVD shapes: Q^T B with Q's rows sharded)
             Q = torch.randn(k, 12, generator=g, dtype=torch.float64)
             got2 = D.crt_matmul_sharded_k(Q[k0:k1].cuda().T, B[k0:k1].cuda())

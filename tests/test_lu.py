@@ -76,3 +76,12 @@ def test_device_panel_transposed_input(monkeypatch):
     A = torch.randn(150, 150, generator=g, dtype=torch.float64).cuda().t()  # column-major view
     (P0, L0, U0), (P1, L1, U1) = _lu_both(A, 64, monkeypatch)
     assert _same_bits(P0, P1) and _same_bits(L0, L1) and _same_bits(U0, U1)
+
+
+@pytest.mark.parametrize("n,block", [(1, 64), (31, 64), (33, 32), (64, 1), (100, 256), (513, 128)])
+def test_device_panel_edge_sizes(monkeypatch, n, block):
+    """Tiny panels, one-column blocks, a block wider than the matrix, a ragged last panel."""
+    g = torch.Generator().manual_seed(100 + n)
+    A = torch.randn(n, n, generator=g, dtype=torch.float64)
+    (P0, L0, U0), (P1, L1, U1) = _lu_both(A.cuda(), block, monkeypatch)
+    assert _same_bits(P0, P1) and _same_bits(L0, L1) and _same_bits(U0, U1)
