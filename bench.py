@@ -2,7 +2,9 @@
 """Benchmark: CRT-emulated float64 GEMM on B200 (emulated TFLOP/s = 2mnk / t).
 
 Workload per GPU: C = A @ B with m = n = k = 8192 float64, entries (U(0,1)-0.5)*exp(phi*N(0,1))
-(phi = 1, seeded), the reference's default modulus count (25 primes at k = 8192).  With N GPUs
+(phi = 1, seeded), 53 bits kept: by default the 16 wide moduli <= 255, whose outputs are
+bit-identical to the reference's 25 primes at k = 8192 (the 25-prime run is timed beside it,
+``reference_moduli``; ``--moduli primes`` makes it the headline).  With N GPUs
 the output is a pr x pc grid of 8192 x 8192 blocks (1x1, 1x2, 2x2, 2x4), one per GPU, each
 rank holding its A row panel and B column panel: the product shards with no data-path
 collective, so per-GPU work is fixed ("scaling": "weak").
@@ -13,7 +15,8 @@ One JSON line on rank 0:
   e2e        the public API crt_matmul() on pinned host tensors: host->device copy of A and B,
              the product, device->host copy of C, all inside the timed region
   roofline   the residue GEMM kernel (K2) timed live with CUDA events between stages:
-             achieved int8 tera-ops/s vs the int8 tensor peak
+             achieved int8 tera-ops/s vs the sustained int8 tensor peak (cuBLAS int8 run
+             back to back for seconds in this process); the burst peak is reported beside it
   cpu_baseline  the CPU oracle (a C restatement of the reference's CPU path) on a sampled
              sub-block at full k, all host threads, rank 0 at N=1 only
 ``--impl reference`` times only that CPU restatement (rank 0; other ranks exit at once).
@@ -113,7 +116,7 @@ def cpu_sample_run(k, s, phi, seed=7):
     return t
 
 
-def calibrate_cpu_sample(k, phi, target_s=4.0):
+def calibrate_cpu_sample(k, phi, target_s=12.0):
     """Largest power-of-two sample edge s (64..2048) whose oracle run stays near target_s."""
     s = 64
     t = cpu_sample_run(k, s, phi)
@@ -123,7 +126,7 @@ def calibrate_cpu_sample(k, phi, target_s=4.0):
     return s
 
 
-def cpu_baseline(k, phi, target_s=4.0, reps=2):
+def cpu_baseline(k, phi, target_s=12.0, reps=3):
     s = calibrate_cpu_sample(k, phi, target_s)
     best = min(cpu_sample_run(k, s, phi) for _ in range(reps))
     return {
@@ -198,6 +201,32 @@ def measure_int8_peak(torch, dev, size=8192, reps=10):
         best = min(best, s.elapsed_time(e))
     del a, b
     return 2.0 * size**3 / (best * 1e-3) / 1e12
+
+
+def measure_int8_sustained(torch, dev, size=8192, seconds=3.0):
+    """cuBLAS int8 GEMM (torch._int_mm) back to back for about `seconds`, tera-ops/s over the
+    last two thirds (the clocks have settled under the power cap by then)."""
+    a = torch.randint(-64, 64, (size, size), dtype=torch.int8, device=dev)
+    b = torch.randint(-64, 64, (size, size), dtype=torch.int8, device=dev)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(5):
+        torch._int_mm(a, b)
+    e.record()
+    e.synchronize()
+    per = s.elapsed_time(e) / 5 * 1e-3
+    lead = max(1, int(seconds / 3 / per))
+    n = max(3, int(seconds * 2 / 3 / per))
+    for _ in range(lead):
+        torch._int_mm(a, b)
+    s.record()
+    for _ in range(n):
+        torch._int_mm(a, b)
+    e.record()
+    e.synchronize()
+    ms = s.elapsed_time(e)
+    del a, b
+    return 2.0 * size**3 * n / (ms * 1e-3) / 1e12
 
 
 def run_reference(args):
@@ -427,19 +456,29 @@ def run_ours(args):
                    "bands compute; C bands copied out as they finish"}
     del Ah, Bh, Ch
 
-    # ---- int8 tensor peak (cuBLAS int8 burst, and 2x the measured bf16 dense peak)
+    # ---- int8 tensor peaks: cuBLAS int8 measured here, and 2x the measured bf16 dense peaks.
+    # The GEMM launches run inside a step loop that lasts about a second, under the power
+    # cap, so the in-step rate is compared with the sustained peak; the solo launch (timed
+    # alone, after a pause) with the burst peak.
     peaks_file = ROOT / "MEASURED_PEAKS.json"
-    bf16 = None
+    bf16 = bf16_sus = None
     if peaks_file.exists():
-        bf16 = json.loads(peaks_file.read_text()).get("bf16_tflops")
-    # only rank 0 prints, so only rank 0 measures the cuBLAS int8 reference
-    int8_cublas = measure_int8_peak(torch, dev) if rank == 0 else None
-    cands = [x for x in (int8_cublas, 2 * bf16 if bf16 else None) if x]
-    peak = max(cands) if cands else 4500.0
-    peak_src = ("max(cuBLAS int8 8192^3 burst measured in this run = "
-                f"{int8_cublas or float('nan'):.0f}, 2 x measured bf16 dense {bf16} = "
-                f"{2 * bf16 if bf16 else float('nan'):.0f}) tera-ops/s" if cands else
-                "fallback: datasheet 4500 dense int8 tera-ops/s")
+        pk = json.loads(peaks_file.read_text())
+        bf16, bf16_sus = pk.get("bf16_tflops"), pk.get("bf16_tflops_sustained")
+    # only rank 0 prints, so only rank 0 measures the cuBLAS int8 references
+    int8_burst = measure_int8_peak(torch, dev) if rank == 0 else None
+    int8_sus = measure_int8_sustained(torch, dev) if rank == 0 else None
+
+    def _pick(own, bf, what):
+        cands = [x for x in (own, 2 * bf if bf else None) if x]
+        if not cands:
+            return 4500.0, "fallback: datasheet 4500 dense int8 tera-ops/s"
+        return max(cands), (f"max(cuBLAS int8 8192^3 {what} measured in this run = "
+                            f"{own or float('nan'):.0f}, 2 x measured bf16 dense {what} {bf} = "
+                            f"{2 * bf if bf else float('nan'):.0f}) tera-ops/s (of measured)")
+
+    peak, peak_src = _pick(int8_sus, bf16_sus, "sustained")
+    peak_burst, peak_burst_src = _pick(int8_burst, bf16, "burst")
     gemm_ops = 2.0 * m * n * k * n_mod
     # in the timed region the GEMM launches (one per row band) run back to back on one
     # stream; their span, from before the first to after the last, includes any wait on a
@@ -450,11 +489,15 @@ def run_ours(args):
             "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
             "traffic": (GEMM_DRAM_BYTES_8192 if (m, n, k) == (8192, 8192, 8192) and n_mod == 16
                         else None),
-            "peak_source": peak_src + " (of measured)",
+            "peak_source": peak_src,
+            "peak_burst": peak_burst, "peak_burst_source": peak_burst_src,
             "ops_per_step": gemm_ops, "gemm_span_ms_per_step": gemm_span,
             "solo_achieved": gemm_ops / (k2 * 1e-3) / 1e12, "solo_ms_per_launch": k2,
+            "solo_frac_of_burst": gemm_ops / (k2 * 1e-3) / 1e12 / peak_burst,
             "note": f"int8 ops: 2*m*n*k per modulus x {n_mod} moduli; unit is tera int8-ops/s; "
-                    "solo_*: one unbanded launch timed alone after the timed region"}
+                    "achieved/frac: the GEMM launches inside the timed step loop against the "
+                    "sustained peak; solo_*: one unbanded launch timed alone after the timed "
+                    "region, against the burst peak"}
     bytes_k1 = (8 * 2 + n_mod) * (m * k + k * n)  # two float64 reads (exp + split) + residues
     bytes_k3 = n_mod * m * n + 8 * m * n
     stages = {"solo_k1_split_ms": k1, "solo_k1_gbs": bytes_k1 / (k1 * 1e-3) / 1e9,
