@@ -226,28 +226,19 @@ static bool make_split_const(const int32_t *moduli, int n_mod, int bits, bool sy
     return true;
 }
 
-// Residue representative on the matmul path.  Floor-mod residues in [0, p) (unsigned bytes,
-// an unsigned residue GEMM) when k * (p_max - 1)^2 leaves the int32 accumulator below
-// 2^31 - 256, which the epilogue's exact reduction needs; otherwise symmetric residues in
-// [-(p-1)/2, (p-1)/2] (signed bytes).  The products mod p, and so every output bit, are the
-// same for either representative; the unsigned form costs the split one operation less per
-// residue.
-static bool floor_mod_residues(const Plan &P, int64_t k) {
-    int64_t pmax = 0;
-    for (int i = 0; i < P.n_mod; ++i) pmax = P.moduli[i] > pmax ? P.moduli[i] : pmax;
-    return k * (pmax - 1) * (pmax - 1) <= (int64_t(1) << 31) - 256;
-}
+// Residue representative on the matmul path: symmetric residues in [-(p-1)/2, (p-1)/2]
+// (signed bytes, a signed residue GEMM).  The products mod p, and so every output bit, are
+// the same for any representative; the symmetric one is the cheaper for the tensor-core
+// split (a rounded float32 quotient) and keeps the GEMM accumulator below k * 127^2.
 
 static bool make_crt_const(const int32_t *moduli, int n_mod, int bits, CrtConst &K);
 
 // Split constants of the matmul path: A's residues carry the CRT factor u_i (so the residue
 // GEMM writes t_i = (u_i A_i B_i) mod p_i with one reduction), B's are plain.
-static bool make_matmul_consts(const Plan &PL, int64_t k, SplitConst &SCA, SplitConst &SCB,
-                               CrtConst &KC) {
-    const bool sym = !floor_mod_residues(PL, k);
+static bool make_matmul_consts(const Plan &PL, SplitConst &SCA, SplitConst &SCB, CrtConst &KC) {
     return make_crt_const(PL.moduli, PL.n_mod, PL.bits, KC) &&
-           make_split_const(PL.moduli, PL.n_mod, PL.bits, sym, KC.u, SCA) &&
-           make_split_const(PL.moduli, PL.n_mod, PL.bits, sym, nullptr, SCB);
+           make_split_const(PL.moduli, PL.n_mod, PL.bits, true, KC.u, SCA) &&
+           make_split_const(PL.moduli, PL.n_mod, PL.bits, true, nullptr, SCB);
 }
 
 // Pairwise-coprime moduli with product below 2^127 (so every lifted value fits 128 bits).
@@ -789,9 +780,9 @@ int ti_crt_matmul_ex(const double *A, int64_t sa0, int64_t sa1, const double *B,
     SplitConst SCA, SC;
     CrtConst KC;
     const Plan &PL = L.plan;
-    // the residue representative follows floor_mod_residues (the products mod p do not
-    // depend on it; the stage entry ti_crt_split keeps the reference's floor-mod bytes)
-    if (!make_matmul_consts(PL, k, SCA, SC, KC)) return TI_ERR_UNSUPPORTED;
+    // symmetric residues (the products mod p do not depend on the representative; the stage
+    // entry ti_crt_split keeps the reference's floor-mod bytes)
+    if (!make_matmul_consts(PL, SCA, SC, KC)) return TI_ERR_UNSUPPORTED;
 
     int bands = opt && opt->bands > 0 ? opt->bands : auto_bands(m);
     if (bands > kMaxBands) bands = kMaxBands;
@@ -933,7 +924,7 @@ int ti_crt_matmul_host(const double *A, int64_t sa0, int64_t sa1, const double *
     if (rc != TI_OK) return rc;
     SplitConst SCA, SC;
     CrtConst KC;
-    if (k > 0 && !make_matmul_consts(L.plan, k, SCA, SC, KC)) return TI_ERR_UNSUPPORTED;
+    if (k > 0 && !make_matmul_consts(L.plan, SCA, SC, KC)) return TI_ERR_UNSUPPORTED;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return TI_ERR_CUDA;
     std::lock_guard<std::mutex> lock(g_pipe[dev].mu);

@@ -11,14 +11,23 @@
 // (m_i the factor folded into the residues, 1 for plain ones),
 //   T_i = sum_j b_j c_(j,i) == m_i v (mod p_i),   0 <= T_i < 8 * 255 * 255 < 2^19,
 // an unsigned 8-bit matrix product with 32-bit accumulation.  G element groups share one
-// MMA through a block-diagonal weight matrix W[(g, i)][(g', j)] = [g == g'] c_(j,i)
-// (M = 128 rows = G groups x 128/G moduli slots, K = 8G bytes) times the digit matrix
-// B[(g', j)][n] = digit j of element (g', n) (N = 256).  D[(g, i)][n] = T_i of element (g, n)
-// lands in TMEM lane g * 128/G + i, so each epilogue thread owns one modulus of one group
-// and reduces consecutive elements of one vector, to the symmetric residue
-//   r = T - p * floor((T + h) / p)  in [-h, h],  h = (p - 1) / 2,
-// or (kFloorMod) to the floor-mod residue r = T - p * floor(T / p) in [0, p), with the
-// quotient umulhi(T (+ h), ceil(2^32 / p)), exact for arguments below 2^24.
+// MMA through a block-diagonal weight matrix W[(i, g)][(g', j)] = [g == g'] c_(j,i)
+// (M = 128 rows = 128/G moduli slots x G groups, row m = i * G + g; K = 8G bytes) times the
+// digit matrix B[(g', j)][n] = digit j of element (g', n) (N = 256).  D[m][n] = T_i of
+// element (g, n) lands in TMEM lane m, so each epilogue thread owns one modulus of one group
+// and reduces consecutive elements of one vector:
+//   symmetric:  r = T - p * round(T / p)  in [-(p-1)/2, (p-1)/2].  The quotient comes from
+//               two float32 operations on pairs of lanes: the bit pattern of T read as a
+//               float32 is the subnormal T * 2^-149; times 2^100 it is T * 2^-49 exactly,
+//               and fma(T * 2^-49, c, 1.5 * 2^23) with c = 2^49 / p rounded to float32
+//               (relative error below 2^-23) rounds T / p (1 + e), |e| < 2^-23, to the
+//               nearest integer q, held as the low bits of 1.5 * 2^23 + q.  That is exact:
+//               T / p is never closer than 1 / (2p) to a half-integer (p is odd) and the
+//               error is below T * 2^-23 / p < 1 / (16 p).  Then
+//               r = T - p * bits(1.5 * 2^23 + q) (mod 2^8), one integer multiply-add,
+//               because bits(1.5 * 2^23) = 0x4B400000 is a multiple of 2^8.
+//   floor-mod:  r = T - p * floor(T / p) in [0, p) with the integer quotient
+//               umulhi(T, ceil(2^32 / p)), exact for arguments below 2^24.
 //
 // G = 8 (up to 16 moduli; K = 64, two MMAs of K = 32) or G = 4 (up to 32 moduli; K = 32).
 // A unit is G vectors x 256 consecutive k: G rows of a k-contiguous operand or G columns of
@@ -26,14 +35,19 @@
 // matrix).  Both operand tiles use the no-swizzle K-major layout: core matrices of 8 rows x
 // 16 bytes, 128 bytes apart along K, 8*K bytes apart along M/N.
 //
+// The residues of a unit leave by TMA: the epilogue writes them to a shared-memory box
+// [modulus][vector][128 k] per half unit, rows of 128 bytes in TMEM-lane order with the
+// 128-byte swizzle (conflict-free for the row-per-lane writes), and one thread stores both
+// halves with 3-D tensor copies that clip rows and columns past the residue planes.
+//
 // Roles (one CTA per SM, persistent over units; vector blocks outer, k blocks fastest):
 //   warp 0       TMA producer: float64 tiles, 4-stage ring.
 //   warp 1       TMEM allocator (512 columns) + MMA issuer, 2 accumulators of 256 columns.
 //   warps 2..9   digits: scale each element, split it into 8 digits, store the B operand
 //                (2-stage ring); two groups of four warps take alternate units.
 //   warps 10..25 epilogue: warp w reads TMEM lane quadrant w % 4, column quarter
-//                (w - 10) / 4; its 32 rows x 64 bytes pass through a private shared-memory
-//                tile so that each store writes whole 64-byte row segments.
+//                (w - 10) / 4, into a double-buffered staging box; warp 10's lane 0 issues
+//                the stores.
 // Every wait is bounded; on timeout the CTA raises an error word, drains its in-flight
 // copies and MMAs, frees TMEM and exits.
 #include <atomic>
@@ -43,8 +57,8 @@
 
 namespace ti {
 
-constexpr int kSpStagePitch = 80;                      // bytes per staged epilogue row
-constexpr int kSpStageWarpBytes = 32 * kSpStagePitch;  // one epilogue warp's 32 rows
+constexpr int kSpBoxBytes = 128 * 128;         // staged residues of half a unit
+constexpr int kSpStageBytes = 2 * kSpBoxBytes;  // one unit
 
 template <int kG>
 struct SplitTcCfg {
@@ -59,7 +73,7 @@ struct SplitTcCfg {
     static constexpr uint32_t kSbo = kK * 8;         // stride of 8-row groups
     static constexpr int kPairs = kG;                // element pairs per digit thread per unit
     static constexpr size_t kUsed = size_t(kXStages) * kXBytes + size_t(kBStages) * kBBytes +
-                                    kWBytes + 16 * kSpStageWarpBytes + 1024 + 256;
+                                    kWBytes + 2 * kSpStageBytes + 1024 + 256;
     // at least 120 KB, so a second CTA (of this kernel, which takes all 512 TMEM columns)
     // never lands on the same SM and waits for TMEM
     static constexpr size_t kSmem = kUsed > 120 * 1024 ? kUsed : 120 * 1024;
@@ -80,6 +94,7 @@ struct SplitTcParams {
     int *err;
     uint32_t p[kMaxModuli];
     uint32_t mult[kMaxModuli];  // factor folded into every residue (1: none)
+    float pinv[kMaxModuli];     // 2^49 / p rounded to float32 (p = 3 in the unused slots)
 };
 
 __device__ __forceinline__ void sp_raise(const SplitTcParams &P, volatile int *abort, int code) {
@@ -123,36 +138,40 @@ __device__ __forceinline__ uint64_t digits8(double x, int bits, int e) {
 
 template <int kG, bool kRows, bool kFloorMod>
 __global__ void __launch_bounds__(kSpThreads, 1)
-    split_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ SplitTcParams P) {
+    split_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmR,
+                    const __grid_constant__ SplitTcParams P) {
     using Cfg = SplitTcCfg<kG>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    // operand tiles first (weights, digits), then the float64 ring and the barriers
+    // operand tiles first (weights, digits), then the float64 ring, the staged residues
+    // (1024-byte aligned: every region before it is a multiple of 1024 bytes) and the barriers
     uint8_t *sW = smem;
     uint8_t *sB = sW + Cfg::kWBytes;
     uint8_t *sX = sB + Cfg::kBStages * Cfg::kBBytes;
-    uint8_t *sE = sX + Cfg::kXStages * Cfg::kXBytes;  // epilogue staging, per warp
-    uint64_t *xfull = reinterpret_cast<uint64_t *>(sE + 16 * kSpStageWarpBytes);
+    uint8_t *sS = sX + Cfg::kXStages * Cfg::kXBytes;  // [2][kSpStageBytes]
+    uint64_t *xfull = reinterpret_cast<uint64_t *>(sS + 2 * kSpStageBytes);
     uint64_t *xempty = xfull + Cfg::kXStages;
     uint64_t *bfull = xempty + Cfg::kXStages;
     uint64_t *bempty = bfull + Cfg::kBStages;
     uint64_t *tfull = bempty + Cfg::kBStages;  // [2]
     uint64_t *tempty = tfull + 2;              // [2]
-    uint64_t *drain = tempty + 2;
+    uint64_t *sfull = tempty + 2;              // [2] staging box written
+    uint64_t *sfree = sfull + 2;               // [2] staging box read by its stores
+    uint64_t *drain = sfree + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-    // weights: row m = g * kSlots + i, column k = g * 8 + j (zero outside the diagonal blocks
+    // weights: row m = i * kG + g, column k = g * 8 + j (zero outside the diagonal blocks
     // and for slots i >= n_mod)
     for (int i = threadIdx.x; i < Cfg::kWBytes / 16; i += blockDim.x)
         reinterpret_cast<uint4 *>(sW)[i] = make_uint4(0u, 0u, 0u, 0u);
     __syncthreads();
     for (int idx = threadIdx.x; idx < 128 * 8; idx += blockDim.x) {
         const int m = idx >> 3, j = idx & 7;
-        const int g = m / Cfg::kSlots, i = m - g * Cfg::kSlots;
+        const int g = m % kG, i = m / kG;
         if (i >= P.n_mod) continue;
         const uint32_t p = P.p[i];
         uint32_t t = 1;
@@ -177,11 +196,14 @@ __global__ void __launch_bounds__(kSpThreads, 1)
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull[a], 1);
             mbar_init(&tempty[a], kSpEpiThreads);
+            mbar_init(&sfull[a], kSpEpiThreads);
+            mbar_init(&sfree[a], 1);
         }
         mbar_init(drain, 1);
         *abort = 0;
         fence_barrier_init();
         prefetch_tensormap(&tmX);
+        prefetch_tensormap(&tmR);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, kSpTmemCols);
@@ -338,35 +360,31 @@ __global__ void __launch_bounds__(kSpThreads, 1)
         // ---------------- epilogue (warps 10..25) ----------------
         const int q = warp & 3;                // TMEM lane quadrant this warp may access
         const int quarter = (warp - 10) >> 2;  // 64-column quarter of the unit
-        const uint32_t p = (q * 32 + lane) % Cfg::kSlots < P.n_mod
-                               ? P.p[(q * 32 + lane) % Cfg::kSlots] : 3u;
-        const uint32_t h = kFloorMod ? 0u : (p >> 1);
+        const int L = q * 32 + lane;           // TMEM lane = weight row m = i * kG + g
+        const int slot = L / kG;               // modulus slot i of this lane
+        const uint32_t p = slot < P.n_mod ? P.p[slot] : 3u;
         const uint32_t magic = static_cast<uint32_t>(((uint64_t(1) << 32) + p - 1) / p);
-        uint8_t *stage = sE + (warp - 10) * kSpStageWarpBytes;
-        // store phase: lane writes 16 bytes of staged row rr = 8*jj + lane/4 for jj = 0..3;
-        // row rr holds TMEM lane q*32 + rr = weight row (g, i)
-        int64_t roff[4];
-        int rg[4];
-        bool rok[4];
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-            const int Lr = q * 32 + 8 * jj + (lane >> 2);
-            const int gr = Lr / Cfg::kSlots, ir = Lr - gr * Cfg::kSlots;
-            rg[jj] = gr;
-            rok[jj] = ir < P.n_mod;
-            roff[jj] = int64_t(ir) * P.plane + int64_t(gr) * P.ld_res + (lane & 3) * 16;
-        }
+        const uint32_t negp = 0u - p;
+        const float2 pinv = make_float2(P.pinv[slot], P.pinv[slot]);
+        const float2 two100 = make_float2(0x1p100f, 0x1p100f);
+        const float2 round23 = make_float2(0x1.8p23f, 0x1.8p23f);
+        // this lane's 128-byte row of its half-unit box; 16-byte chunk j of the row sits at
+        // chunk j ^ (L & 7) (the store's 128-byte swizzle; L & 7 == lane & 7)
+        const int box = quarter >> 1, chunk0 = (quarter & 1) * 4;
+        const bool issuer = warp == 10 && lane == 0;
         int64_t local = 0;
         for (GridIter it(P.k_blocks); it.a < P.vec_blocks; it.next(), ++local) {
-            const int acc = static_cast<int>(local & 1);
+            const int acc = static_cast<int>(local & 1);  // accumulator and staging buffer
             const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
-            if (!mbar_wait(&tfull[acc], acc_phase, abort)) {
+            if (!mbar_wait(&tfull[acc], acc_phase, abort) ||
+                !mbar_wait(&sfree[acc], acc_phase ^ 1, abort)) {
                 sp_raise(P, abort, kErrTimeoutEpilogue);
                 break;
             }
             tc_fence_after();
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(acc) * 256u + quarter * 64;
+            uint8_t *row = sS + acc * kSpStageBytes + box * kSpBoxBytes + L * 128;
 #pragma unroll 1
             for (int c = 0; c < 2; ++c) {
                 uint32_t v[32];
@@ -380,31 +398,49 @@ __global__ void __launch_bounds__(kSpThreads, 1)
 #pragma unroll
                 for (int w = 0; w < 8; ++w) {
                     uint32_t r[4];
+                    if (kFloorMod) {
 #pragma unroll
-                    for (int b = 0; b < 4; ++b) {
-                        const uint32_t T = v[4 * w + b];
-                        r[b] = T - __umulhi(kFloorMod ? T : T + h, magic) * p;  // low byte
+                        for (int b = 0; b < 4; ++b) {
+                            const uint32_t T = v[4 * w + b];
+                            r[b] = T - __umulhi(T, magic) * p;  // low byte
+                        }
+                    } else {
+#pragma unroll
+                        for (int b = 0; b < 4; b += 2) {
+                            const float2 x = make_float2(__uint_as_float(v[4 * w + b]),
+                                                         __uint_as_float(v[4 * w + b + 1]));
+                            const float2 qv = __ffma2_rn(__fmul2_rn(x, two100), pinv, round23);
+                            r[b] = v[4 * w + b] + negp * __float_as_uint(qv.x);  // low byte
+                            r[b + 1] = v[4 * w + b + 1] + negp * __float_as_uint(qv.y);
+                        }
                     }
                     pk[w] = __byte_perm(__byte_perm(r[0], r[1], 0x0040),
                                         __byte_perm(r[2], r[3], 0x0040), 0x5410);
                 }
-                uint4 *row = reinterpret_cast<uint4 *>(stage + lane * kSpStagePitch + c * 32);
-                row[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                row[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                const int j0 = chunk0 + 2 * c;
+                *reinterpret_cast<uint4 *>(row + ((j0 ^ (lane & 7)) << 4)) =
+                    make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                *reinterpret_cast<uint4 *>(row + (((j0 + 1) ^ (lane & 7)) << 4)) =
+                    make_uint4(pk[4], pk[5], pk[6], pk[7]);
             }
-            __syncwarp();
-            const int64_t o0 = it.a * kG;
-            const int64_t l0 = it.b * Cfg::kN + quarter * 64 + (lane & 3) * 16;
-            const int64_t base = o0 * P.ld_res + it.b * Cfg::kN + quarter * 64;
-#pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-                const uint4 val = *reinterpret_cast<const uint4 *>(
-                    stage + (8 * jj + (lane >> 2)) * kSpStagePitch + (lane & 3) * 16);
-                if (rok[jj] && o0 + rg[jj] < P.outer && l0 < P.ld_res)
-                    *reinterpret_cast<uint4 *>(P.res + base + roff[jj]) = val;
+            fence_proxy_async_smem();  // staged residues before the copy engine reads them
+            mbar_arrive(&sfull[acc]);
+            if (issuer) {
+                if (!mbar_wait(&sfull[acc], acc_phase, abort)) {
+                    sp_raise(P, abort, kErrTimeoutEpilogue);
+                    break;
+                }
+                const int x0 = static_cast<int>(it.b * Cfg::kN);
+                const int y0 = static_cast<int>(it.a * kG);
+                uint8_t *box0 = sS + acc * kSpStageBytes;
+                tma_store_3d(&tmR, box0, x0, y0, 0);
+                if (x0 + 128 < P.ld_res) tma_store_3d(&tmR, box0 + kSpBoxBytes, x0 + 128, y0, 0);
+                bulk_commit_group();
+                bulk_wait_group_read<1>();  // the previous unit's boxes are read
+                if (local > 0) mbar_arrive(&sfree[acc ^ 1]);
             }
-            __syncwarp();  // the staged rows are read before the next unit overwrites them
         }
+        if (issuer) bulk_wait_group<0>();  // every store complete before the CTA exits
     }
 
     tc_fence_before();
@@ -417,8 +453,8 @@ __global__ void __launch_bounds__(kSpThreads, 1)
 }
 
 template <int kG, bool kRows, bool kFloorMod>
-static cudaError_t launch_split_tc_t(const CUtensorMap &tm, const SplitTcParams &P, int num_sms,
-                                     cudaStream_t stream) {
+static cudaError_t launch_split_tc_t(const CUtensorMap &tm, const CUtensorMap &tr,
+                                     const SplitTcParams &P, int num_sms, cudaStream_t stream) {
     static std::atomic<int> configured{-1};  // last device configured
     int dev = 0;
     cudaGetDevice(&dev);
@@ -432,7 +468,7 @@ static cudaError_t launch_split_tc_t(const CUtensorMap &tm, const SplitTcParams 
     const int64_t units = P.vec_blocks * P.k_blocks;
     const int64_t grid = units < num_sms ? units : num_sms;
     split_tc_kernel<kG, kRows, kFloorMod><<<static_cast<unsigned>(grid), kSpThreads,
-                                            SplitTcCfg<kG>::kSmem, stream>>>(tm, P);
+                                            SplitTcCfg<kG>::kSmem, stream>>>(tm, tr, P);
     return cudaGetLastError();
 }
 
@@ -452,7 +488,8 @@ cudaError_t launch_split_tc(const double *X, int64_t outer, int64_t kdim, int64_
     if (C.n_mod > kMaxModuli || kdim < 1 ||
         (reinterpret_cast<uintptr_t>(X) & 15) || (stride & 1) || stride < 2 ||
         stride >= (int64_t(1) << 36) || (!rows && s_outer != 1) || (ld_res & 15) ||
-        (plane & 15) || (reinterpret_cast<uintptr_t>(res) & 15))
+        (plane & 15) || (reinterpret_cast<uintptr_t>(res) & 15) || ld_res >= (int64_t(1) << 30) ||
+        outer >= (int64_t(1) << 30) || plane >= (int64_t(1) << 39))
         return cudaErrorNotSupported;
     const EncodeTiledFn enc = get_encode_fn();
     if (!enc) return cudaErrorNotSupported;
@@ -468,6 +505,20 @@ cudaError_t launch_split_tc(const double *X, int64_t outer, int64_t kdim, int64_
             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return cudaErrorNotSupported;
+    // residue planes [modulus][outer][ld_res] bytes, stored by boxes of 128 k x G vectors x
+    // all moduli
+    CUtensorMap tr;
+    const cuuint64_t rdims[3] = {static_cast<cuuint64_t>(ld_res), static_cast<cuuint64_t>(outer),
+                                 static_cast<cuuint64_t>(C.n_mod)};
+    const cuuint64_t rstrides[2] = {static_cast<cuuint64_t>(ld_res),
+                                    static_cast<cuuint64_t>(plane)};
+    const cuuint32_t rbox[3] = {128u, static_cast<cuuint32_t>(G),
+                                static_cast<cuuint32_t>(C.n_mod)};
+    const cuuint32_t restr[3] = {1, 1, 1};
+    if (enc(&tr, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, res, rdims, rstrides, rbox, restr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return cudaErrorNotSupported;
     SplitTcParams P;
     std::memset(&P, 0, sizeof(P));
     P.outer = outer;
@@ -481,13 +532,15 @@ cudaError_t launch_split_tc(const double *X, int64_t outer, int64_t kdim, int64_
     P.bits = C.bits;
     P.n_mod = C.n_mod;
     P.err = err;
-    for (int i = 0; i < C.n_mod; ++i) {
-        P.p[i] = C.mm.p[i];
-        P.mult[i] = C.mult[i];
+    for (int i = 0; i < kMaxModuli; ++i) {
+        const uint32_t pi = i < C.n_mod ? C.mm.p[i] : 3u;
+        P.p[i] = i < C.n_mod ? pi : 0u;
+        P.mult[i] = i < C.n_mod ? C.mult[i] : 0u;
+        P.pinv[i] = static_cast<float>(0x1p49 / static_cast<double>(pi));
     }
 #define TI_SPLIT_TC(GG, FM)                                                               \
-    return rows ? launch_split_tc_t<GG, true, FM>(tm, P, num_sms, stream)                 \
-                : launch_split_tc_t<GG, false, FM>(tm, P, num_sms, stream);
+    return rows ? launch_split_tc_t<GG, true, FM>(tm, tr, P, num_sms, stream)             \
+                : launch_split_tc_t<GG, false, FM>(tm, tr, P, num_sms, stream);
     if (G == 8) {
         if (C.symmetric) { TI_SPLIT_TC(8, false) }
         TI_SPLIT_TC(8, true)
