@@ -24,8 +24,8 @@
 //   warp 0       TMA producer, 5-stage ring of 16 KB stages.
 //   warp 1       TMEM allocator (256 columns) + single-thread MMA issuer: 4 MMAs of
 //                128 x 32 x 32 per unit into one of 2 accumulator buffers.
-//   warps 2..17  epilogue: warp w reads TMEM lane quadrant w % 4 of row (w - 2) / 4 of the
-//                unit, one output per thread.
+//   warps 2..9   epilogue: warp w reads TMEM lane quadrant w % 4 of rows (w - 2) / 4 and
+//                (w - 2) / 4 + 2 of the unit, two outputs per thread.
 // Every wait is bounded; on timeout the CTA raises an error word, drains its in-flight
 // copies and MMAs, frees TMEM and exits.
 #include <atomic>
@@ -46,9 +46,13 @@ constexpr int kTcWBytes = kTcN * 128;                 // W: 32 K-major rows of 1
 constexpr int kTcAcc = 2;                             // TMEM accumulator buffers
 constexpr uint32_t kTcAccCols = kTcRows * kTcN;       // 128 columns per buffer
 constexpr uint32_t kTcTmemCols = kTcAcc * kTcAccCols; // 256: two CTAs per SM share TMEM
-constexpr int kTcEpiWarps = 4 * kTcRows;              // 16
-constexpr int kTcEpiThreads = 32 * kTcEpiWarps;       // 512
-constexpr int kTcThreads = 64 + kTcEpiThreads;        // 576
+#ifndef TI_CRT_TC_ROWS_PER_THREAD
+#define TI_CRT_TC_ROWS_PER_THREAD 2
+#endif
+constexpr int kTcRowsPerThread = TI_CRT_TC_ROWS_PER_THREAD;  // outputs per epilogue thread
+constexpr int kTcEpiWarps = 4 * kTcRows / kTcRowsPerThread;  // one per lane quadrant and row set
+constexpr int kTcEpiThreads = 32 * kTcEpiWarps;
+constexpr int kTcThreads = 64 + kTcEpiThreads;
 // Two CTAs fit on one SM (2 x 85 KB of shared memory, 2 x 256 TMEM columns); with the
 // residue GEMM (194 KB) a CTA never shares an SM, so TMEM is never oversubscribed.
 constexpr size_t kTcSmemBytes = size_t(kTcStages) * kTcStageBytes + kTcWBytes + 1024 + 256;
@@ -310,14 +314,39 @@ __global__ void __launch_bounds__(kTcThreads, 2)
             }
         }
     } else {
-        // ---------------- epilogue (warps 2..17) ----------------
-        const int r = (warp - 2) >> 2;  // row of the unit
-        const int q = warp & 3;         // TMEM lane quadrant this warp may access
-        const int m = q * 32 + lane;    // column within the unit (TMEM lane)
+        // ---------------- epilogue (warps 2 .. 2 + kTcEpiWarps) ----------------
+        // warp w reads TMEM lane quadrant w % 4 (the unit's columns 32q .. 32q + 31) for the
+        // rows r0, r0 + kRowStep, ... of the unit, one output per row and thread.  The
+        // exponents of the next unit are loaded while this one is reconstructed.
+        constexpr int kRowStep = kTcRows / kTcRowsPerThread;
+        const int r0 = (warp - 2) >> 2;
+        const int q = warp & 3;
+        const int m = q * 32 + lane;  // column within the unit (TMEM lane)
         const CrtConst &K = P.K;
+        GridIter it(P.col_blocks);
+        while (it.a < P.row_blocks && tc_skip(P, it.a, it.b)) it.next();
+        int ce_n = kNonfiniteExp, re_n[kTcRowsPerThread];
+        auto load_exps = [&](const GridIter &u) {
+            const int64_t col = u.b * kTcCols + m;
+            ce_n = col < P.cols ? __ldg(P.col_exp + col) : kNonfiniteExp;
+#pragma unroll
+            for (int k = 0; k < kTcRowsPerThread; ++k) {
+                const int64_t row = u.a * kTcRows + r0 + k * kRowStep;
+                re_n[k] = row < P.rows ? __ldg(P.row_exp + row) : kNonfiniteExp;
+            }
+        };
+        if (it.a < P.row_blocks) load_exps(it);
         int64_t local = 0;
-        for (GridIter it(P.col_blocks); it.a < P.row_blocks; it.next()) {
-            if (tc_skip(P, it.a, it.b)) continue;
+        while (it.a < P.row_blocks) {
+            const int64_t ua = it.a, ub = it.b;
+            const int ce = ce_n;
+            int re[kTcRowsPerThread];
+#pragma unroll
+            for (int k = 0; k < kTcRowsPerThread; ++k) re[k] = re_n[k];
+            do {
+                it.next();
+            } while (it.a < P.row_blocks && tc_skip(P, it.a, it.b));
+            if (it.a < P.row_blocks) load_exps(it);
             const int acc = static_cast<int>(local % kTcAcc);
             const uint32_t acc_phase = static_cast<uint32_t>((local / kTcAcc) & 1);
             ++local;
@@ -326,23 +355,30 @@ __global__ void __launch_bounds__(kTcThreads, 2)
                 break;
             }
             tc_fence_after();
-            uint32_t D[32];
-            tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                                   static_cast<uint32_t>(acc) * kTcAccCols + r * kTcN,
-                               D);
+            const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                                  static_cast<uint32_t>(acc) * kTcAccCols;
+            uint32_t D[kTcRowsPerThread][32];
+#pragma unroll
+            for (int k = 0; k < kTcRowsPerThread; ++k)
+                tmem_ld_32x32b_x32(tacc + (r0 + k * kRowStep) * kTcN, D[k]);
             tmem_wait_ld();
             tc_fence_before();
             mbar_arrive(&tempty[acc]);
-            const int64_t row = it.a * kTcRows + r, col = it.b * kTcCols + m;
-            if (row >= P.rows || col >= P.cols) continue;
-            const int re = P.row_exp[row], ce = P.col_exp[col];
-            const double v = (re == kNonfiniteExp || ce == kNonfiniteExp)
-                                 ? nan_value()
-                                 : crt_from_byte_sums(D, re + ce - K.two_bits, K);
-            double *dst = P.C + row * P.ldc + col;
-            if (kOutMode == 0) *dst = v;
-            else if (kOutMode == 1) *dst = __dsub_rn(*dst, v);
-            else *dst = __dadd_rn(*dst, v);
+            const int64_t col = ub * kTcCols + m;
+#pragma unroll
+            for (int k = 0; k < kTcRowsPerThread; ++k) {
+                const int64_t row = ua * kTcRows + r0 + k * kRowStep;
+                if (row >= P.rows || col >= P.cols) continue;
+                double *dst = P.C + row * P.ldc + col;
+                double old = 0.0;
+                if (kOutMode != 0) old = *dst;
+                const double v = (re[k] == kNonfiniteExp || ce == kNonfiniteExp)
+                                     ? nan_value()
+                                     : crt_from_byte_sums(D[k], re[k] + ce - K.two_bits, K);
+                if (kOutMode == 0) *dst = v;
+                else if (kOutMode == 1) *dst = __dsub_rn(old, v);
+                else *dst = __dadd_rn(old, v);
+            }
         }
     }
 
