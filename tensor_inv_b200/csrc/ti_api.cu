@@ -329,7 +329,7 @@ static int cuda_status(cudaError_t e) { return e == cudaSuccess ? TI_OK : TI_ERR
 // ---------------------------------------------------------------------------------------
 // per-device streams and events of the banded pipeline (created once, kept until exit)
 // ---------------------------------------------------------------------------------------
-constexpr int kMaxBands = 8;
+constexpr int kMaxBands = 16;
 constexpr int kMaxDevices = 64;
 constexpr int kSideBlocksPerSm = 2;  // split/CRT blocks per SM while a GEMM is resident
 
@@ -836,23 +836,29 @@ int ti_crt_matmul_ex(const double *A, int64_t sa0, int64_t sa1, const double *B,
 // One row band of C = A @ B, all stages in order on `s`, inside the workspace laid out for
 // the full product (L).  B's exponents and residues are produced when split_b and reused by
 // the following bands.
-static int crt_band_compute(const double *A, int64_t sa0, int64_t sa1, const double *B,
-                            int64_t sb0, int64_t sb1, double *C, int64_t ldc, int64_t rows,
-                            int64_t n, int64_t k, const CrtLayout &L, const SplitConst &SCA,
-                            const SplitConst &SC,
-                            const CrtConst &KC, uint8_t *ws, cudaStream_t s, bool split_b,
-                            const DevInfo &d) {
+// B's column exponents and residues (once per product, before the first band).
+static int crt_split_b(const double *B, int64_t sb0, int64_t sb1, int64_t n, int64_t k,
+                       const CrtLayout &L, const SplitConst &SC, uint8_t *ws, cudaStream_t s,
+                       const DevInfo &d) {
+    int32_t *cexp = reinterpret_cast<int32_t *>(ws + L.off_cexp);
+    int8_t *bres = reinterpret_cast<int8_t *>(ws + L.off_b);
+    const cudaError_t e =
+        sb0 == 1 ? launch_split(B, n, k, sb1, 1, SC, cexp, bres, L.ldk, d.num_sms, s, 0, 8, d.err)
+                 : launch_split(B, n, k, 1, sb0, SC, cexp, bres, L.ldk, d.num_sms, s, 0, 8, d.err);
+    return cuda_status(e);
+}
+
+// One row band of C = A @ B, B already split (crt_split_b).
+static int crt_band_compute(const double *A, int64_t sa0, int64_t sa1, double *C, int64_t ldc,
+                            int64_t rows, int64_t n, int64_t k, const CrtLayout &L,
+                            const SplitConst &SCA, const SplitConst &SC, const CrtConst &KC,
+                            uint8_t *ws, cudaStream_t s, const DevInfo &d) {
     int32_t *rexp = reinterpret_cast<int32_t *>(ws + L.off_rexp);
     int32_t *cexp = reinterpret_cast<int32_t *>(ws + L.off_cexp);
     int8_t *ares = reinterpret_cast<int8_t *>(ws + L.off_a);
     int8_t *bres = reinterpret_cast<int8_t *>(ws + L.off_b);
     uint8_t *R = ws + L.off_r;
     cudaError_t e;
-    if (split_b) {
-        if (sb0 == 1) e = launch_split(B, n, k, sb1, 1, SC, cexp, bres, L.ldk, d.num_sms, s, 0, 8, d.err);
-        else e = launch_split(B, n, k, 1, sb0, SC, cexp, bres, L.ldk, d.num_sms, s, 0, 8, d.err);
-        if (e != cudaSuccess) return TI_ERR_CUDA;
-    }
     if (sa1 == 1) e = launch_split(A, rows, k, sa0, 1, SCA, rexp, ares, L.ldk, d.num_sms, s, 0, 8, d.err);
     else e = launch_split(A, rows, k, 1, sa1, SCA, rexp, ares, L.ldk, d.num_sms, s, 0, 8, d.err);
     if (e != cudaSuccess) return TI_ERR_CUDA;
@@ -886,6 +892,43 @@ int ti_crt_host_workspace_size(int64_t m, int64_t n, int64_t k, int bits,
     if (rc != TI_OK) return rc;
     *bytes = total;
     return TI_OK;
+}
+
+// Row bands of the host-operand pipeline: band b is rows [r0[b], r0[b] + rows[b]).  The
+// copies are PCIe-bound: all of B, then A, in; C out.  C starts out once B and A's first band
+// are in and computed, and ends after A's last band is in, computed and out; while A comes in,
+// C goes out at the same byte rate, about one band behind.  So for m >= 4096 the first band
+// is short (256 rows), the middle ones about 1024 rows and the last ones shrink (512, 256,
+// 128 rows) to shorten the tail.  n > 0 in options.bands asks for n equal bands instead.
+// Returns the band count.
+static int host_bands(int64_t m, const ti_crt_options_t *opt, int64_t (&r0)[kMaxBands],
+                      int64_t (&rows)[kMaxBands]) {
+    int count = 0;
+    auto push = [&](int64_t r) {
+        r0[count] = count ? r0[count - 1] + rows[count - 1] : 0;
+        rows[count++] = r;
+    };
+    auto equal = [&](int nb) {
+        if (nb > kMaxBands) nb = kMaxBands;
+        if (nb < 1) nb = 1;
+        int64_t br = (m + nb - 1) / nb;
+        br = (br + 127) / 128 * 128;
+        for (int64_t r = 0; r < m; r += br) push(m - r < br ? m - r : br);
+        return count;
+    };
+    if (opt && opt->bands > 0) return equal(opt->bands);
+    if (m < 1024) return equal(1);
+    if (m < 4096) return equal(4);
+    constexpr int64_t kHead = 256, kTail[3] = {512, 256, 128};
+    const int64_t mid = m - kHead - (kTail[0] + kTail[1] + kTail[2]);
+    int64_t nmid = (mid + 1023) / 1024;
+    if (nmid > kMaxBands - 4) nmid = kMaxBands - 4;
+    int64_t br = (mid + nmid - 1) / nmid;
+    br = (br + 127) / 128 * 128;
+    push(kHead);
+    for (int64_t r = 0; r < mid; r += br) push(mid - r < br ? mid - r : br);
+    for (int64_t t : kTail) push(t);
+    return count;
 }
 
 // Host band copy of rows [r0, r0+rows) of an m x k operand with strides (s0, s1), one of
@@ -940,13 +983,8 @@ int ti_crt_matmul_host(const double *A, int64_t sa0, int64_t sa1, const double *
     // device strides of the dense copies (same orientation as the host operands)
     const int64_t da0 = (sa1 == 1) ? k : 1, da1 = (sa1 == 1) ? 1 : m;
     const int64_t db0 = (sb1 == 1) ? n : 1, db1 = (sb1 == 1) ? 1 : k;
-    // PCIe-bound: more bands shorten the tail after the last copy in (8 x 1024 rows at
-    // 8192^3: 23.6 ms against 25.5 ms for 4 bands and 38.7 ms for one)
-    int bands = opt && opt->bands > 0 ? opt->bands : (m >= 4096 ? 8 : (m >= 1024 ? 4 : 1));
-    if (bands > kMaxBands) bands = kMaxBands;
-    int64_t band_rows = (m + bands - 1) / bands;
-    band_rows = (band_rows + 127) / 128 * 128;
-    bands = static_cast<int>((m + band_rows - 1) / band_rows);
+    int64_t band_r0[kMaxBands], band_rows[kMaxBands];
+    const int bands = host_bands(m, opt, band_r0, band_rows);
 
     if (cudaEventRecord(P.fork, s) != cudaSuccess ||
         cudaStreamWaitEvent(P.h2d, P.fork, 0) != cudaSuccess ||
@@ -961,24 +999,25 @@ int ti_crt_matmul_host(const double *A, int64_t sa0, int64_t sa1, const double *
                                 sizeof(double) * k, n, cudaMemcpyHostToDevice, P.h2d);
         if (e != cudaSuccess || cudaEventRecord(P.b_in, P.h2d) != cudaSuccess) return TI_ERR_CUDA;
         for (int b = 0; b < bands; ++b) {
-            const int64_t r0 = int64_t(b) * band_rows;
-            const int64_t rows = m - r0 < band_rows ? m - r0 : band_rows;
+            const int64_t r0 = band_r0[b], rows = band_rows[b];
             if (copy_rows_h2d(dA, A, m, k, sa0, sa1, r0, rows, P.h2d) != cudaSuccess ||
                 cudaEventRecord(P.a_in[b], P.h2d) != cudaSuccess)
                 return TI_ERR_CUDA;
         }
+        // B is split as soon as it is in, while A's first band is still arriving
         if (cudaStreamWaitEvent(s, P.b_in, 0) != cudaSuccess) return TI_ERR_CUDA;
+        rc = crt_split_b(dB, db0, db1, n, k, L, SC, ws + off_ws, s, d);
+        if (rc != TI_OK) return rc;
     }
     // kernels on the caller's stream, one band at a time; each band's C goes out as soon as
     // it is reconstructed
     for (int b = 0; b < bands; ++b) {
-        const int64_t r0 = int64_t(b) * band_rows;
-        const int64_t rows = m - r0 < band_rows ? m - r0 : band_rows;
+        const int64_t r0 = band_r0[b], rows = band_rows[b];
         if (k > 0) {
             if (cudaStreamWaitEvent(s, P.a_in[b], 0) != cudaSuccess) return TI_ERR_CUDA;
-            // band b of C = A[r0:r0+rows] @ B, with B split only once (in the first band)
-            rc = crt_band_compute(dA + r0 * da0, da0, da1, dB, db0, db1, dC + r0 * n, n, rows, n,
-                                  k, L, SCA, SC, KC, ws + off_ws, s, b == 0, d);
+            // band b of C = A[r0:r0+rows] @ B
+            rc = crt_band_compute(dA + r0 * da0, da0, da1, dC + r0 * n, n, rows, n, k, L, SCA,
+                                  SC, KC, ws + off_ws, s, d);
             if (rc != TI_OK) return rc;
         } else if (cudaMemsetAsync(dC + r0 * n, 0, sizeof(double) * rows * n, s) != cudaSuccess) {
             return TI_ERR_CUDA;  // empty sum

@@ -558,6 +558,19 @@ def test_host_pipeline_matches_device_path(ti, pinned, moduli):
     _assert_bitexact(C, want.cpu().numpy())
 
 
+@pytest.mark.parametrize("b_colmajor", [False, True])
+def test_host_pipeline_uneven_bands(ti, b_colmajor):
+    """m >= 4096: a 256-row first band, ~1024-row middle bands and 512/256/128-row last
+    bands (m = 4100: 256, 1024, 1024, 900, 512, 256, 128); B split before A's first band."""
+    m, n, k = 4100, 200, 160
+    A = _rand((m, k), 171, 1.0).pin_memory()
+    B = _rand((k, n), 172, 1.0)
+    B = B.T.contiguous().pin_memory().T if b_colmajor else B.pin_memory()
+    C = ti.crt_matmul(A, B, moduli="wide")
+    want = ti.crt_matmul(A.cuda(), B.cuda(), moduli="wide")
+    _assert_bitexact(C, want.cpu().numpy())
+
+
 def test_host_pipeline_transposed_views(ti, oracle):
     A = _rand((300, 900), 141, 0.5).T     # 900 x 300, column-major view
     B = _rand((250, 300), 142, 0.5).T     # 300 x 250, column-major view
