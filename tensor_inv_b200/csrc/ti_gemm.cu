@@ -29,6 +29,7 @@
 //
 // Every wait is bounded; on timeout the CTA raises an error word, drains its in-flight
 // copies and MMAs, frees TMEM and exits.
+#include <cstdlib>
 #include <cstring>
 
 #include "ti_crt_math.cuh"
@@ -479,7 +480,7 @@ EncodeTiledFn get_encode_fn() {
 
 // 3-D map over int8 residue planes [planes][rows][ld] with dims (kdim, rows, planes) and a
 // box of (128, box_rows, 1) using the 128-byte swizzle.
-static bool make_plane_map(CUtensorMap *map, const void *base, int64_t kdim, int64_t rows,
+bool make_plane_map(CUtensorMap *map, const void *base, int64_t kdim, int64_t rows,
                            int64_t ld, int64_t planes, int box_rows, int64_t plane_stride) {
     EncodeTiledFn enc = get_encode_fn();
     if (!enc) return false;
@@ -533,6 +534,23 @@ static cudaError_t fill_common(GemmParams &P, CUtensorMap &tmA, CUtensorMap &tmB
 
 int gemm_smem_bytes() { return static_cast<int>(kGemmSmemBytes); }
 
+cudaError_t launch_residue_gemm_pair(const int8_t *a_res, const int8_t *b_res, int64_t m,
+                                     int64_t n, int64_t kdim, int64_t ld, int n_mod,
+                                     const ModMagic &mm, void *out, int64_t ldo, int out_i32,
+                                     int *err, cudaStream_t stream, int64_t a_plane,
+                                     int64_t b_plane, int64_t out_plane, const uint32_t *weights,
+                                     bool unsigned_ops, bool lower);
+
+// The CTA-pair kernel (ti_gemm2.cu) takes products with K >= 1024 and at least one 256 x 256
+// tile; shorter K loops (the trailing updates of LU and Cholesky) are bounded by the
+// epilogue, where the one-CTA kernel's eight epilogue warps serve better.  TI_GEMM_PAIR=0
+// in the environment selects the one-CTA kernel throughout.
+static bool use_pair_kernel(int64_t m, int64_t n, int64_t kdim) {
+    const char *env = std::getenv("TI_GEMM_PAIR");
+    if (env && env[0] == '0') return false;
+    return kdim >= 1024 && m >= 256 && n >= 256;
+}
+
 // Launch R[i] = (A_i @ B_i^T) mod p_i over n_mod planes.
 //   a_res: [n_mod][m][ld] int8, b_res: [n_mod][n][ld] int8 (K-major, ld % 16 == 0)
 //   out:   uint8 [n_mod][m][ldo] (ldo % 16 == 0) or int32 [n_mod][m][ldo]
@@ -550,6 +568,13 @@ cudaError_t launch_residue_gemm(const int8_t *a_res, const int8_t *b_res, int64_
                                 int64_t out_plane, const uint32_t *weights, bool unsigned_ops,
                                 bool lower) {
     if (m == 0 || n == 0 || n_mod == 0) return cudaSuccess;
+    if (use_pair_kernel(m, n, kdim)) {
+        const cudaError_t pe = launch_residue_gemm_pair(a_res, b_res, m, n, kdim, ld, n_mod, mm,
+                                                        out, ldo, out_i32, err, stream, a_plane,
+                                                        b_plane, out_plane, weights, unsigned_ops,
+                                                        lower);
+        if (pe != cudaErrorNotSupported) return pe;
+    }
     int dev = 0;
     cudaGetDevice(&dev);
     cudaError_t e = configure<false>(dev);

@@ -624,3 +624,69 @@ def test_lower_update_matches_full_on_lower_triangle(ti, monkeypatch, n, k, k3):
     ti.crt_matmul_update(low, L21, L21.T, alpha=-1, moduli="wide", lower=True)
     mask = torch.ones(n, n, dtype=torch.bool, device="cuda").tril()
     assert torch.equal(full[mask].view(torch.int64), low[mask].view(torch.int64))
+
+
+# ---------------------------------------------------------------------------------------
+# residue GEMM on CTA pairs (tcgen05.mma.cta_group::2, K >= 1024) against the one-CTA kernel
+# ---------------------------------------------------------------------------------------
+def _both_gemm_kernels(monkeypatch, fn):
+    monkeypatch.setenv("TI_GEMM_PAIR", "1")
+    got = fn()
+    torch.cuda.synchronize()
+    monkeypatch.setenv("TI_GEMM_PAIR", "0")
+    want = fn()
+    torch.cuda.synchronize()
+    monkeypatch.delenv("TI_GEMM_PAIR")
+    return got, want
+
+
+@pytest.mark.parametrize("m,n,k,moduli", [
+    (256, 256, 1024, "wide"), (300, 700, 1100, None), (257, 513, 2048, None),
+    (1000, 260, 1024, "wide"), (129, 1030, 4100, "wide"),
+])
+def test_pair_gemm_matches_one_cta(ti, monkeypatch, m, n, k, moduli):
+    A = _rand((m, k), 181, 1.0).cuda()
+    B = _rand((k, n), 182, 1.0).cuda()
+    got, want = _both_gemm_kernels(monkeypatch, lambda: ti.crt_matmul(A, B, moduli=moduli))
+    _assert_bitexact(got, want.cpu().numpy())
+
+
+def test_pair_gemm_lower_update(ti, monkeypatch):
+    n, k = 700, 1024
+    L = _rand((n, k), 191).cuda()
+    C0 = _rand((n, n), 192).cuda()
+
+    def upd():
+        C = C0.clone()
+        ti.crt_matmul_update(C, L, L.T, alpha=-1, moduli="wide", lower=True)
+        return C
+
+    got, want = _both_gemm_kernels(monkeypatch, upd)
+    _assert_bitexact(torch.tril(got), torch.tril(want).cpu().numpy())
+
+
+def test_pair_gemm_int32_partials(ti, monkeypatch):
+    """ti_crt_residue_partial writes int32 residue products (the sharded-k path)."""
+    from tensor_inv_b200 import _native as nat
+
+    m, n, k, n_mod, bits = 300, 260, 1100, 25, 53
+    A = _rand((m, k), 201, 1.0).cuda()
+    B = _rand((k, n), 202, 1.0).cuda()
+    cm = importlib.import_module("tensor_inv_b200.crt_matmul")
+    re, _ = cm._split(A, bits, n_mod, axis_k=1)
+    ce, _ = cm._split(B, bits, n_mod, axis_k=0)
+
+    def partial():
+        out = torch.zeros((n_mod, m, n), dtype=torch.int32, device="cuda")
+        ws_b = ctypes.c_size_t(0)
+        nat.check("ws", nat.lib().ti_crt_residue_partial_workspace_size(m, n, k, n_mod,
+                                                                      ctypes.byref(ws_b)))
+        ws = torch.empty(max(ws_b.value, 256), dtype=torch.uint8, device="cuda")
+        nat.check("partial", nat.lib().ti_crt_residue_partial(
+            A.data_ptr(), k, 1, B.data_ptr(), n, 1, m, n, k, bits, n_mod,
+            re.int().contiguous().data_ptr(), ce.int().contiguous().data_ptr(), out.data_ptr(),
+            ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream))
+        return out
+
+    got, want = _both_gemm_kernels(monkeypatch, partial)
+    assert torch.equal(got, want)
