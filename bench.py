@@ -40,10 +40,11 @@ sys.path.insert(0, str(ROOT))
 METRIC = "emulated FP64 GEMM TFLOP/s at 8192³, 1/2/4/8 B200; % of int8 TC peak"
 UNIT = "TFLOP/s"
 GRIDS = {1: (1, 1), 2: (1, 2), 4: (2, 2), 8: (2, 4)}
-# dram__bytes_read.sum + dram__bytes_write.sum of one residue-GEMM launch at 8192^3 with the 16
-# wide moduli (5,299,600,384 + 1,059,266,304 bytes), from the 1-pass ncu launch list summarised
-# in profiles/launches_crt_matmul_8192.md.
-GEMM_DRAM_BYTES_8192 = 6358866688
+# dram__bytes_read.sum + dram__bytes_write.sum of one residue-GEMM launch (the CTA-pair kernel)
+# at 8192^3 with the 16 wide moduli: the mean of three launches (6.59 GB read + 1.06 GB
+# written each), from the 1-pass ncu launch list summarised in
+# profiles/launches_crt_matmul_8192.md.
+GEMM_DRAM_BYTES_8192 = 7657961813
 
 
 def parse_args():
@@ -485,10 +486,13 @@ def run_ours(args):
     # band's split, so this rate is a lower bound of the kernel's own
     gemm_span = piped["gemms_ms"]
     achieved = gemm_ops / (gemm_span * 1e-3) / 1e12
-    roof = {"bound": "tensor", "kernel": "residue_gemm_kernel (K2, tcgen05 kind::i8)",
+    pair = os.environ.get("TI_GEMM_PAIR", "1")[:1] != "0" and k >= 1024 and m >= 256 and n >= 256
+    kname = ("residue_gemm_pair_kernel (K2, tcgen05.mma.cta_group::2 kind::i8, CTA pairs)" if pair
+             else "residue_gemm_kernel (K2, tcgen05.mma kind::i8)")
+    roof = {"bound": "tensor", "kernel": kname,
             "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
             "traffic": (GEMM_DRAM_BYTES_8192 if (m, n, k) == (8192, 8192, 8192) and n_mod == 16
-                        else None),
+                        and pair else None),
             "peak_source": peak_src,
             "peak_burst": peak_burst, "peak_burst_source": peak_burst_src,
             "ops_per_step": gemm_ops, "gemm_span_ms_per_step": gemm_span,

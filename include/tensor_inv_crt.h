@@ -269,6 +269,19 @@ int ti_lu_panel_workspace_size(size_t *bytes);
 int ti_lu_panel(double *W, int64_t ldw, int64_t n, int64_t j, int64_t jb, int64_t *piv,
                 void *workspace, size_t workspace_bytes, void *stream);
 
+/*
+ * ti_lu_panel on a panel that sits at any column of a rectangular W: the panel is rows
+ * [j, n) of W's columns [pc, pc + jb - j), W has n rows and `ncols` columns (leading
+ * dimension ldw >= ncols), and every row swap exchanges all ncols columns.  Column k of the
+ * reference loop is W's column pc + (k - j); rows keep their global indices, as do piv's
+ * entries.  ti_lu_panel(W, ldw, n, j, jb, ...) is ti_lu_panel_ex(W, ldw, n, n, j, jb, j, ...).
+ * It serves a rank that holds only some block columns of the matrix (the block-cyclic LU of
+ * tensor_inv_b200.distributed): the panel owner factorises its panel in its local columns.
+ */
+int ti_lu_panel_ex(double *W, int64_t ldw, int64_t n, int64_t ncols, int64_t j, int64_t jb,
+                   int64_t pc, int64_t *piv, void *workspace, size_t workspace_bytes,
+                   void *stream);
+
 #ifdef __cplusplus
 }
 #endif

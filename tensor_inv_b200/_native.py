@@ -76,6 +76,7 @@ SIGNATURES = {
                                       _int, _p, _p, _p, _p, _sz, _p]),
     "ti_lu_panel_workspace_size": (_int, [ctypes.POINTER(_sz)]),
     "ti_lu_panel": (_int, [_p, _i64, _i64, _i64, _i64, _p, _p, _sz, _p]),
+    "ti_lu_panel_ex": (_int, [_p, _i64, _i64, _i64, _i64, _i64, _i64, _p, _p, _sz, _p]),
 }
 
 _lib = None
@@ -214,3 +215,12 @@ def lu_panel(W, j: int, jb: int, piv, workspace, stream) -> None:
     check("ti_lu_panel", lib().ti_lu_panel(W.data_ptr(), W.stride(0), n, j, jb, piv.data_ptr(),
                                            workspace.data_ptr(), workspace.numel(),
                                            stream.cuda_stream))
+
+
+def lu_panel_cols(W, j: int, jb: int, pc: int, piv, workspace, stream) -> None:
+    """The LU panel of rows [j, n) held in columns [pc, pc + jb - j) of the row-major float64
+    CUDA tensor W (n rows, any column count); row swaps exchange all of W's columns."""
+    n, ncols = W.shape
+    check("ti_lu_panel_ex", lib().ti_lu_panel_ex(W.data_ptr(), W.stride(0), n, ncols, j, jb, pc,
+                                                 piv.data_ptr(), workspace.data_ptr(),
+                                                 workspace.numel(), stream.cuda_stream))

@@ -4,7 +4,7 @@
 // same order, so P, L and U are bit-identical to the reference's torch loop:
 //   for k in [j, jb):
 //     p = first index of the maximum of |W[i, k]| over i >= k    (torch argmax)
-//     if p != k: swap rows k and p of W (all n columns) and entries k and p of piv
+//     if p != k: swap rows k and p of W (all its columns) and entries k and p of piv
 //     if |W[k, k]| > 1e-15:
 //       W[i, k] = W[i, k] / W[k, k]                            for i > k
 //       W[i, c] = W[i, c] - round(W[i, k] * W[k, c])           for i > k, k < c < jb
@@ -141,8 +141,9 @@ __device__ __forceinline__ void lu_global_pivot(const LuCand *cands, unsigned G,
 }
 
 __global__ void __launch_bounds__(kLuThreads)
-    lu_panel_kernel(double *__restrict__ W, int64_t ldw, int64_t n, int64_t j, int64_t jb,
-                    int64_t *__restrict__ piv, LuSync *sync, LuCand *cand, int *err) {
+    lu_panel_kernel(double *__restrict__ W, int64_t ldw, int64_t n, int64_t ncols, int64_t j,
+                    int64_t jb, int64_t dc, int64_t *__restrict__ piv, LuSync *sync, LuCand *cand,
+                    int *err) {
     __shared__ double urow[kLuMaxPanel];  // W[k, k+1 .. jb-1] of the current column
     __shared__ double red_v[kLuThreads / 32];
     __shared__ long long red_i[kLuThreads / 32];
@@ -162,7 +163,7 @@ __global__ void __launch_bounds__(kLuThreads)
         double bv = -1.0;
         long long bi = LLONG_MAX;
         for (int64_t i = (r0 > k ? r0 : k) + tid; i < r1; i += kLuThreads) {
-            const double v = fabs(__ldcg(W + i * ldw + k));
+            const double v = fabs(__ldcg(W + i * ldw + k + dc));
             if (bi == LLONG_MAX || lu_better(v, i, bv, bi)) {
                 bv = v;
                 bi = i;
@@ -198,9 +199,9 @@ __global__ void __launch_bounds__(kLuThreads)
         lu_global_pivot(cand, G, &piv_row, &piv_cta, red_v, red_i, red_b);
         const int64_t p = piv_row;
         if (p != k) {
-            const int64_t per_c = (n + G - 1) / G;
+            const int64_t per_c = (ncols + G - 1) / G;
             const int64_t c0 = int64_t(blockIdx.x) * per_c;
-            const int64_t c1 = c0 + per_c < n ? c0 + per_c : n;
+            const int64_t c1 = c0 + per_c < ncols ? c0 + per_c : ncols;
             for (int64_t c = c0 + tid; c < c1; c += kLuThreads) {
                 const double a = __ldcg(W + k * ldw + c), b = __ldcg(W + p * ldw + c);
                 __stcg(W + k * ldw + c, b);
@@ -215,13 +216,14 @@ __global__ void __launch_bounds__(kLuThreads)
         if (!lu_grid_sync(sync, G, gen, err)) return;
 
         // ---- C: scale column k and update the panel, owned rows > k
-        const double d = __ldcg(W + k * ldw + k);
+        const double d = __ldcg(W + k * ldw + k + dc);
         if (!(fabs(d) > 1e-15)) continue;  // the reference skips this column
         const int64_t nc = jb - k - 1;
-        for (int64_t c = tid; c < nc; c += kLuThreads) urow[c] = __ldcg(W + k * ldw + k + 1 + c);
+        for (int64_t c = tid; c < nc; c += kLuThreads)
+            urow[c] = __ldcg(W + k * ldw + k + dc + 1 + c);
         __syncthreads();
         for (int64_t i = (r0 > k + 1 ? r0 : k + 1) + warp; i < r1; i += kLuThreads / 32) {
-            double *wi = W + i * ldw;
+            double *wi = W + i * ldw + dc;  // panel column k of row i at wi[k]
             const double l = __ddiv_rn(__ldcg(wi + k), d);
             for (int64_t c0 = 0; c0 < nc; c0 += 256) {  // 8 loads in flight per lane
                 double x[8];
@@ -263,8 +265,9 @@ struct LuSlots {
 };
 
 __global__ void __launch_bounds__(kLuThreads)
-    lu_panel_smem_kernel(double *__restrict__ W, int64_t ldw, int64_t n, int64_t j, int64_t jb,
-                         int64_t *__restrict__ piv, LuSync *sync, LuSlots *slots, int *err) {
+    lu_panel_smem_kernel(double *__restrict__ W, int64_t ldw, int64_t n, int64_t ncols, int64_t j,
+                         int64_t jb, int64_t col0, int64_t *__restrict__ piv, LuSync *sync,
+                         LuSlots *slots, int *err) {
     extern __shared__ double P[];            // [per][b + 1]: owned rows, panel columns
     __shared__ double urow[kLuSmemMaxPanel];  // the pivot row (after the swap), panel columns
     __shared__ double red_v[kLuThreads / 32];
@@ -283,10 +286,10 @@ __global__ void __launch_bounds__(kLuThreads)
 
     for (int e = tid; e < nr * b; e += kLuThreads) {
         const int r = e / b, c = e - r * b;
-        P[r * pitch + c] = __ldcg(W + (r0 + r) * ldw + j + c);
+        P[r * pitch + c] = __ldcg(W + (r0 + r) * ldw + col0 + c);
     }
     // columns outside the panel, this CTA's slice of them (for the row swaps)
-    const int64_t nout = n - b;
+    const int64_t nout = ncols - b;
     const int64_t per_c = (nout + G - 1) / G;
     const int64_t t0 = int64_t(blockIdx.x) * per_c;
     const int64_t t1 = t0 + per_c < nout ? t0 + per_c : nout;
@@ -343,17 +346,17 @@ __global__ void __launch_bounds__(kLuThreads)
         // ---- B: the global pivot, the pivot row, the swap
         lu_global_pivot(slots->cand[par], G, &piv_row, &piv_cta, red_v, red_i, red_b);
         const int64_t p = piv_row;
-        const int pc = piv_cta;
-        for (int c = tid; c < b; c += kLuThreads) urow[c] = __ldcg(&slots->crow[par][pc][c]);
+        const int pcta = piv_cta;
+        for (int c = tid; c < b; c += kLuThreads) urow[c] = __ldcg(&slots->crow[par][pcta][c]);
         if (p != k) {
             if (k >= r0 && k < r1)  // row k takes old row p
                 for (int c = tid; c < b; c += kLuThreads)
-                    P[(k - r0) * pitch + c] = __ldcg(&slots->crow[par][pc][c]);
+                    P[(k - r0) * pitch + c] = __ldcg(&slots->crow[par][pcta][c]);
             if (p >= r0 && p < r1)  // row p takes old row k
                 for (int c = tid; c < b; c += kLuThreads)
                     P[(p - r0) * pitch + c] = __ldcg(&slots->krow[par][c]);
             for (int64_t t = t0 + tid; t < t1; t += kLuThreads) {
-                const int64_t c = t < j ? t : t + b;
+                const int64_t c = t < col0 ? t : t + b;
                 const double x = __ldcg(W + k * ldw + c), y = __ldcg(W + p * ldw + c);
                 __stcg(W + k * ldw + c, y);
                 __stcg(W + p * ldw + c, x);
@@ -383,7 +386,7 @@ __global__ void __launch_bounds__(kLuThreads)
 
     for (int e = tid; e < nr * b; e += kLuThreads) {
         const int r = e / b, c = e - r * b;
-        __stcg(W + (r0 + r) * ldw + j + c, P[r * pitch + c]);
+        __stcg(W + (r0 + r) * ldw + col0 + c, P[r * pitch + c]);
     }
 }
 
@@ -412,9 +415,16 @@ int ti_lu_panel_workspace_size(size_t *bytes) {
 
 int ti_lu_panel(double *W, int64_t ldw, int64_t n, int64_t j, int64_t jb, int64_t *piv,
                 void *workspace, size_t workspace_bytes, void *stream) {
-    if (!W || !piv || n < 1 || ldw < n || j < 0 || jb <= j || jb > n ||
-        jb - j > kLuMaxPanel)
+    return ti_lu_panel_ex(W, ldw, n, n, j, jb, j, piv, workspace, workspace_bytes, stream);
+}
+
+int ti_lu_panel_ex(double *W, int64_t ldw, int64_t n, int64_t ncols, int64_t j, int64_t jb,
+                   int64_t pc, int64_t *piv, void *workspace, size_t workspace_bytes,
+                   void *stream) {
+    if (!W || !piv || n < 1 || ncols < 1 || ldw < ncols || j < 0 || jb <= j || jb > n ||
+        jb - j > kLuMaxPanel || pc < 0 || pc + (jb - j) > ncols)
         return TI_ERR_INVALID_ARGUMENT;
+    int64_t dc = pc - j;  // column shift of the panel (a kernel argument, so not const)
     size_t need = 0;
     ti_lu_panel_workspace_size(&need);
     if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255))
@@ -461,7 +471,7 @@ int ti_lu_panel(double *W, int64_t ldw, int64_t n, int64_t j, int64_t jb, int64_
                                                           kLuThreads, smem) == cudaSuccess &&
             int64_t(per_sm_s) * num_sms >= g_smem) {
             LuSlots *slots = reinterpret_cast<LuSlots *>(ws + lu_slots_offset());
-            void *args[] = {&W, &ldw, &n, &j, &jb, &piv, &sync, &slots, &err};
+            void *args[] = {&W, &ldw, &n, &ncols, &j, &jb, &pc, &piv, &sync, &slots, &err};
             if (cudaLaunchCooperativeKernel(reinterpret_cast<const void *>(lu_panel_smem_kernel),
                                             dim3(static_cast<unsigned>(g_smem)), dim3(kLuThreads),
                                             args, smem, s) != cudaSuccess)
@@ -470,7 +480,7 @@ int ti_lu_panel(double *W, int64_t ldw, int64_t n, int64_t j, int64_t jb, int64_
         }
     }
     LuCand *cand = reinterpret_cast<LuCand *>(ws + lu_cand_offset());
-    void *args[] = {&W, &ldw, &n, &j, &jb, &piv, &sync, &cand, &err};
+    void *args[] = {&W, &ldw, &n, &ncols, &j, &jb, &dc, &piv, &sync, &cand, &err};
     if (cudaLaunchCooperativeKernel(reinterpret_cast<const void *>(lu_panel_kernel),
                                     dim3(static_cast<unsigned>(grid)), dim3(kLuThreads), args, 0,
                                     s) != cudaSuccess)

@@ -21,6 +21,7 @@ A's rows sharded, built on it.
 
 from __future__ import annotations
 
+import importlib
 import math
 
 import torch
@@ -272,3 +273,225 @@ def rsvd_rows(A_local, rank, n_oversamples=10, n_power_iter=1, *, group=None):
     U_local = _mm(Q_local, Ub)
 
     return U_local[:, :rank], S[:rank], Vt[:rank]
+
+
+# ---------------------------------------------------------------------------------------
+# Block-cyclic LU and Cholesky: block column c (columns [c*b, c*b + b)) lives on rank
+# c % world.  Each step broadcasts the panel from its owner and updates every rank's own
+# trailing columns, so the results are bit-identical to ``lu`` / ``cholesky`` on one GPU.
+# ---------------------------------------------------------------------------------------
+def cyclic_blocks(n: int, block_size: int, rank: int, world: int) -> list[int]:
+    """Block-column indices owned by `rank` when block c goes to rank c % world."""
+    return list(range(rank, -(-n // block_size), world))
+
+
+def cyclic_columns(n: int, block_size: int, rank: int, world: int) -> torch.Tensor:
+    """Global column indices held by `rank`, in the order of its local columns."""
+    cols = [torch.arange(c * block_size, min(n, (c + 1) * block_size))
+            for c in cyclic_blocks(n, block_size, rank, world)]
+    return torch.cat(cols) if cols else torch.zeros(0, dtype=torch.long)
+
+
+def _exact_sum_(X, group):
+    """All-reduce of a float64 tensor in which every element is nonzero on at most one rank:
+    summing the int64 bit patterns (x + 0 is x for every pattern) copies each value exactly."""
+    import torch.distributed as dist
+
+    dist.all_reduce(X.view(torch.int64), group=group)
+    return X
+
+
+def _global_rank(group, rank):
+    import torch.distributed as dist
+
+    return rank if group is None else dist.get_global_rank(group, rank)
+
+
+def _panel_torch_cols(W, piv, j, jb, pc):
+    """The reference's unblocked panel (lu.py:24-34) with the panel's column k held in W's
+    column pc + k - j; row swaps exchange all of W's columns."""
+    c1 = pc + jb - j
+    for k in range(j, jb):
+        ck = pc + k - j
+        max_idx = W[k:, ck].abs().argmax() + k
+        if max_idx != k:
+            W[k], W[max_idx] = W[max_idx].clone(), W[k].clone()
+            piv[k], piv[max_idx] = piv[max_idx].clone(), piv[k].clone()
+
+        if W[k, ck].abs() > 1e-15:
+            W[k + 1:, ck] /= W[k, ck]
+            W[k + 1:, ck + 1:c1] -= W[k + 1:, ck:ck + 1] @ W[k:k + 1, ck + 1:c1]
+
+
+def _trailing_update(Wv, A, B, k, matmul, lower=False):
+    """Wv -= A @ B through the CRT kernels (fused into the reconstruction on CUDA), or through
+    `matmul` when given."""
+    from tensor_inv_b200.crt_matmul import caller_moduli, crt_matmul, crt_matmul_update
+
+    if matmul is not None:
+        Wv -= matmul(A, B)
+    elif Wv.is_cuda and Wv.dtype == torch.float64 and Wv.stride(1) == 1:
+        crt_matmul_update(Wv, A, B, alpha=-1, moduli=caller_moduli(k), lower=lower)
+    else:
+        Wv -= crt_matmul(A, B, moduli=caller_moduli(k))
+
+
+def lu_cyclic(W_local, n: int, block_size: int = 64, *, group=None, matmul=None):
+    """Blocked LU with partial pivoting (lu.py:6-54) on block-cyclic columns.
+
+    W_local holds this rank's block columns of the n x n matrix (``cyclic_columns``), all n
+    rows.  Per block column: its owner factorises the panel (``ti_lu_panel_ex`` on CUDA
+    float64, else the reference's torch loop) with row swaps across its local columns, then
+    broadcasts the pivot vector and the panel; the other ranks apply the same row permutation
+    to their columns.  The U block row is assembled exactly from every rank's columns and
+    solved whole on each rank (the reference's call, so the same bits), and each rank updates
+    its own trailing columns: a column subset of the reference's product, which the CRT
+    kernels compute bit for bit (column exponents depend on their column only).  Returns this
+    rank's factored columns and the pivot vector (the same on every rank)."""
+    import torch.distributed as dist
+
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    b = block_size
+    W = W_local.clone()
+    dev = W.device
+    mine = cyclic_blocks(n, b, rank, world)
+    local_off = {c: i * b for i, c in enumerate(mine)}
+    piv = torch.arange(n, device=dev)
+    lu_mod = importlib.import_module("tensor_inv_b200.lu")  # the module, not the function
+    device_panel = W.is_cuda and W.dtype == torch.float64 and not lu_mod._TORCH_PANEL
+    if device_panel:
+        from tensor_inv_b200 import _native as nat
+
+        ws = torch.empty(nat.lu_panel_workspace_size(), dtype=torch.uint8, device=dev)
+        stream = torch.cuda.current_stream(dev)
+    for j in range(0, n, b):
+        c = j // b
+        bw = min(b, n - j)
+        jb = j + bw
+        owner = c % world
+        if rank == owner:
+            lc = local_off[c]
+            if device_panel and bw <= 1024:
+                nat.lu_panel_cols(W, j, jb, lc, piv, ws, stream)
+            else:
+                _panel_torch_cols(W, piv, j, jb, lc)
+            panel = W[j:, lc:lc + bw].contiguous()
+            new_piv = piv.clone()
+        else:
+            panel = torch.empty((n - j, bw), dtype=W.dtype, device=dev)
+            new_piv = torch.empty_like(piv)
+        src = _global_rank(group, owner)
+        dist.broadcast(new_piv, src=src, group=group)
+        dist.broadcast(panel, src=src, group=group)
+        if rank != owner:
+            # the owner's row swaps, as one permutation of rows j.. (piv moved with the rows)
+            pos = torch.empty_like(piv)
+            pos[piv] = torch.arange(n, device=dev)
+            W[j:] = W[pos[new_piv[j:]]]
+            piv = new_piv
+        if jb < n:
+            L_panel = torch.tril(panel[:bw], diagonal=-1) + torch.eye(bw, dtype=W.dtype,
+                                                                       device=dev)
+            later = [c2 for c2 in mine if c2 > c]
+            row = torch.zeros((bw, n - jb), dtype=W.dtype, device=dev)
+            if later:
+                lo = local_off[later[0]]
+                gcols = torch.cat([torch.arange(c2 * b, min(n, (c2 + 1) * b))
+                                   for c2 in later]).to(dev) - jb
+                row[:, gcols] = W[j:jb, lo:]
+            _exact_sum_(row, group)
+            # triangular solve for the U block row (lu.py:38-43), whole on every rank
+            U = torch.linalg.solve_triangular(L_panel, row, upper=False)
+            if later:
+                U_mine = U[:, gcols]
+                W[j:jb, lo:] = U_mine
+                # trailing update of this rank's columns (lu.py:46)
+                _trailing_update(W[jb:, lo:], panel[bw:], U_mine, bw, matmul)
+    return W, piv
+
+
+def lu_distributed(A, block_size: int = 64, *, group=None, matmul=None):
+    """``lu(A, block_size)`` computed block-cyclically over the ranks of `group`; every rank
+    passes the same A and gets the same P, L, U as one GPU's ``lu``, bit for bit."""
+    import torch.distributed as dist
+
+    if A.shape[0] != A.shape[1]:
+        raise ValueError(f"expected square matrix, got {A.shape}")
+    n = A.shape[0]
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    cols = cyclic_columns(n, block_size, rank, world).to(A.device)
+    W_local, piv = lu_cyclic(A[:, cols].contiguous(), n, block_size, group=group,
+                             matmul=matmul)
+    W = torch.zeros((n, n), dtype=A.dtype, device=A.device)
+    W[:, cols] = W_local
+    _exact_sum_(W, group)
+    L = torch.tril(W, diagonal=-1) + torch.eye(n, dtype=A.dtype, device=A.device)
+    U = torch.triu(W)
+    P = torch.zeros(n, n, dtype=A.dtype, device=A.device)
+    P[torch.arange(n, device=A.device), piv] = 1.0
+    return P, L, U
+
+
+def cholesky_cyclic(A_local, n: int, block_size: int = 64, *, group=None, matmul=None):
+    """Blocked right-looking Cholesky (cholesky.py:6-35) on block-cyclic columns.
+
+    The owner of a block column computes its diagonal block's Cholesky factor and the panel
+    below it (the reference's calls), broadcasts the panel, and every rank updates its own
+    trailing columns with W[:, cols] -= L21 @ L21[cols]^T (all rows below the panel: the
+    lower-triangle tile skip of one GPU needs whole columns).  The factor's values are the
+    reference's bit for bit.  Returns this rank's columns of L."""
+    import torch.distributed as dist
+
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    b = block_size
+    W = A_local.clone()
+    L = torch.zeros_like(W)
+    dev = W.device
+    mine = cyclic_blocks(n, b, rank, world)
+    local_off = {c: i * b for i, c in enumerate(mine)}
+    for j in range(0, n, b):
+        c = j // b
+        bw = min(b, n - j)
+        jb = j + bw
+        owner = c % world
+        if rank == owner:
+            lc = local_off[c]
+            # panel: small Cholesky on the diagonal block (cholesky.py:24)
+            L[j:jb, lc:lc + bw] = torch.linalg.cholesky(W[j:jb, lc:lc + bw])
+            if jb < n:
+                # triangular solve for the sub-diagonal block (cholesky.py:28-30)
+                L[jb:, lc:lc + bw] = torch.linalg.solve_triangular(
+                    L[j:jb, lc:lc + bw], W[jb:, lc:lc + bw].T, upper=False
+                ).T
+        if jb >= n:
+            break
+        if rank == owner:
+            L21 = L[jb:, lc:lc + bw].contiguous()
+        else:
+            L21 = torch.empty((n - jb, bw), dtype=W.dtype, device=dev)
+        dist.broadcast(L21, src=_global_rank(group, owner), group=group)
+        later = [c2 for c2 in mine if c2 > c]
+        if later:
+            lo = local_off[later[0]]
+            gcols = torch.cat([torch.arange(c2 * b, min(n, (c2 + 1) * b))
+                               for c2 in later]).to(dev) - jb
+            # trailing update of this rank's columns (cholesky.py:33)
+            _trailing_update(W[jb:, lo:], L21, L21[gcols].T, bw, matmul)
+    return L
+
+
+def cholesky_distributed(A, block_size: int = 64, *, group=None, matmul=None):
+    """``cholesky(A, block_size)`` computed block-cyclically over the ranks of `group`; every
+    rank passes the same A and gets the same L as one GPU's ``cholesky``, bit for bit."""
+    import torch.distributed as dist
+
+    if A.shape[0] != A.shape[1]:
+        raise ValueError(f"expected square matrix, got {A.shape}")
+    n = A.shape[0]
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    cols = cyclic_columns(n, block_size, rank, world).to(A.device)
+    L_local = cholesky_cyclic(A[:, cols].contiguous(), n, block_size, group=group,
+                              matmul=matmul)
+    L = torch.zeros((n, n), dtype=A.dtype, device=A.device)
+    L[:, cols] = L_local
+    return _exact_sum_(L, group)

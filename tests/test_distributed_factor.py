@@ -1,0 +1,124 @@
+"""Block-cyclic LU and Cholesky (tensor_inv_b200.distributed) against one process.
+
+CPU tests: world sizes 2 and 3 on gloo, trailing products through the CPU oracle (an exact
+CRT product, so each output depends only on its own row and column, as on the GPU); every
+rank compares the distributed P, L, U (or L) with a world-size-1 run of the same code.
+GPU tests: two gloo ranks on one GPU against ``lu`` / ``cholesky`` of the whole matrix.
+"""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _same(a, b):
+    return torch.equal(a.contiguous().view(torch.int64), b.contiguous().view(torch.int64))
+
+
+def _matrix(kind, n, seed, device="cpu"):
+    g = torch.Generator().manual_seed(seed)
+    X = torch.randn(n, n, generator=g, dtype=torch.float64)
+    if kind == "spd":
+        X = X @ X.T / n + 1e-3 * torch.eye(n, dtype=torch.float64)
+    elif kind == "ties":
+        X = torch.randint(-3, 4, (n, n), generator=g).to(torch.float64)
+    return X.to(device)
+
+
+def _cpu_worker(rank, world, port, kind, n, block, errs):
+    import torch.distributed as dist
+
+    from oracle import oracle
+    from tensor_inv_b200 import distributed as D
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        def mm(a, b):
+            return torch.from_numpy(oracle.crt_matmul(a.contiguous().numpy(),
+                                                      b.contiguous().numpy(), 53))
+
+        singles = [dist.new_group([r]) for r in range(world)]  # collective: every rank
+        A = _matrix(kind, n, 40 + n)
+        if kind == "spd":
+            got = D.cholesky_distributed(A, block, matmul=mm)
+            want = D.cholesky_distributed(A, block, group=singles[rank], matmul=mm)
+            ok = _same(got, want)
+        else:
+            P, L, U = D.lu_distributed(A, block, matmul=mm)
+            P1, L1, U1 = D.lu_distributed(A, block, group=singles[rank], matmul=mm)
+            ok = _same(P, P1) and _same(L, L1) and _same(U, U1)
+            if kind == "randn":
+                ok = ok and float((P @ A - L @ U).abs().max()) < 1e-10 * float(A.abs().max())
+        if not ok:
+            errs.put(f"rank {rank}: {kind} n={n} b={block} differs")
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("kind,n,block", [("randn", 50, 8), ("ties", 40, 8), ("spd", 45, 8),
+                                          ("randn", 16, 32)])
+def test_cyclic_factorizations_match_one_process(oracle, world, kind, n, block):
+    ctx = mp.get_context("spawn")
+    errs = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_cpu_worker, args=(r, world, port, kind, n, block, errs))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert errs.empty(), errs.get()
+
+
+def test_cyclic_columns_partition():
+    from tensor_inv_b200 import distributed as D
+
+    n, b = 70, 8
+    for world in (1, 2, 3, 4):
+        cols = torch.cat([D.cyclic_columns(n, b, r, world) for r in range(world)])
+        assert sorted(cols.tolist()) == list(range(n))
+        for r in range(world):
+            assert all((c // b) % world == r for c in D.cyclic_columns(n, b, r, world).tolist())
+
+
+def _gpu_worker(rank, world, port, kind, n, block):
+    import torch.distributed as dist
+
+    import tensor_inv_b200 as ti
+    from tensor_inv_b200 import distributed as D
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        torch.cuda.set_device(0)
+        A = _matrix(kind, n, 70 + n, "cuda")
+        if kind == "spd":
+            got = D.cholesky_distributed(A, block)
+            assert _same(got, ti.cholesky(A, block_size=block)), "cholesky differs"
+        else:
+            P, L, U = D.lu_distributed(A, block)
+            P1, L1, U1 = ti.lu(A, block_size=block)
+            assert _same(P, P1) and _same(L, L1) and _same(U, U1), "lu differs"
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("kind,n,block", [("randn", 700, 64), ("ties", 300, 64),
+                                          ("spd", 650, 64), ("randn", 1300, 256)])
+def test_cyclic_factorizations_gpu_match_one_gpu(kind, n, block):
+    mp.spawn(_gpu_worker, args=(2, _free_port(), kind, n, block), nprocs=2, join=True)

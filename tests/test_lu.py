@@ -85,3 +85,25 @@ def test_device_panel_edge_sizes(monkeypatch, n, block):
     A = torch.randn(n, n, generator=g, dtype=torch.float64)
     (P0, L0, U0), (P1, L1, U1) = _lu_both(A.cuda(), block, monkeypatch)
     assert _same_bits(P0, P1) and _same_bits(L0, L1) and _same_bits(U0, U1)
+
+
+@pytest.mark.parametrize("n,ncols,j,b,pc", [
+    (700, 380, 0, 64, 0), (700, 380, 128, 64, 64), (700, 380, 640, 60, 320),
+    (300, 500, 40, 64, 300), (900, 600, 100, 300, 150),   # b > 256: the global-memory kernel
+])
+def test_panel_at_shifted_columns(n, ncols, j, b, pc):
+    """ti_lu_panel_ex: the panel of rows [j, n) in columns [pc, pc + b) of a rectangular W,
+    row swaps across all of W's columns, equals the reference loop with shifted columns."""
+    from tensor_inv_b200 import _native as nat
+    from tensor_inv_b200 import distributed as D
+
+    g = torch.Generator().manual_seed(n + j)
+    W0 = torch.randn(n, ncols, generator=g, dtype=torch.float64).cuda()
+    Wt, pt = W0.clone(), torch.arange(n, device="cuda")
+    D._panel_torch_cols(Wt, pt, j, j + b, pc)
+    Wd, pd = W0.clone(), torch.arange(n, device="cuda")
+    ws = torch.empty(nat.lu_panel_workspace_size(), dtype=torch.uint8, device="cuda")
+    nat.lu_panel_cols(Wd, j, j + b, pc, pd, ws, torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    assert torch.equal(pt, pd) and _same_bits(Wt, Wd)
+    assert nat.device_error(reset=True) == 0
