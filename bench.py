@@ -66,7 +66,7 @@ def parse_args():
     p.add_argument("--workload", choices=["gemm", "lu", "cholesky", "rsvd"], default="gemm",
                    help="gemm: the CRT GEMM line (default); lu / cholesky / rsvd: the callers "
                         "of the CRT GEMM timed end to end with their backward errors")
-    p.add_argument("--n", type=int, default=None, help="matrix order (lu, cholesky) or rows "
+    p.add_argument("--order", type=int, default=None, help="matrix order (lu, cholesky) or rows "
                    "(rsvd); default 16384 / 16384 / 65536")
     return p.parse_args()
 
@@ -565,8 +565,13 @@ def run_factorization(args):
 
     line = {"workload": args.workload, "data": "synthetic, seeded, generated on the device",
             "device": torch.cuda.get_device_name(dev)}
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1:
+        if args.workload not in ("lu", "cholesky"):
+            raise SystemExit("--workload rsvd runs on one GPU (rsvd_rows is tested, not timed)")
+        return run_factorization_cyclic(args, dev, line, world)
     if args.workload == "lu":
-        n = args.n or 16384
+        n = args.order or 16384
         A = torch.randn(n, n, generator=g, dtype=torch.float64, device=dev)
         (P, L, U), t = timed(lambda: ti.lu(A, block_size=256))
         err = (torch.linalg.norm(P @ A - L @ U) / torch.linalg.norm(A)).item()
@@ -576,7 +581,7 @@ def run_factorization(args):
                      "trailing_update_tflop": sum(2.0 * (n - j) ** 2 * 256
                                                   for j in range(256, n, 256)) / 1e12})
     elif args.workload == "cholesky":
-        n = args.n or 16384
+        n = args.order or 16384
         X = torch.randn(n, n, generator=g, dtype=torch.float64, device=dev)
         A = X @ X.T / n + 1e-6 * torch.eye(n, dtype=torch.float64, device=dev)
         del X
@@ -586,7 +591,7 @@ def run_factorization(args):
         line.update({"n": n, "block": 256, "seconds": t, "backward_error_fro": err,
                      "torch_cholesky_seconds": t_ref})
     else:
-        m = args.n or 65536
+        m = args.order or 65536
         n, r = 8192, 256
         Uq, _ = torch.linalg.qr(torch.randn(m, r, generator=g, dtype=torch.float64, device=dev))
         Vq, _ = torch.linalg.qr(torch.randn(n, r, generator=g, dtype=torch.float64, device=dev))
@@ -600,6 +605,62 @@ def run_factorization(args):
         line.update({"m": m, "n": n, "rank": r, "oversampling": 10, "power_iterations": 2,
                      "seconds": t, "relative_error_fro": err, "max_singular_value_error": sv_err})
     print(json.dumps(line), flush=True)
+
+
+def run_factorization_cyclic(args, dev, line, world):
+    """Block-cyclic LU / Cholesky over the ranks (tensor_inv_b200.distributed): every rank
+    builds the same matrix, the factorisation is timed with a barrier and a device sync on both
+    sides (second of two calls, max over ranks), and rank 0 checks the gathered factors bit for
+    bit against the one-GPU routine."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import tensor_inv_b200 as ti
+    from tensor_inv_b200 import distributed as D
+
+    dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=180))
+    rank = dist.get_rank()
+    try:
+        n = args.order or 16384
+        g = torch.Generator(device=dev).manual_seed(0)
+        X = torch.randn(n, n, generator=g, dtype=torch.float64, device=dev)
+        if args.workload == "cholesky":
+            A = X @ X.T / n + 1e-6 * torch.eye(n, dtype=torch.float64, device=dev)
+            run = lambda: D.cholesky_distributed(A, block_size=256)  # noqa: E731
+        else:
+            A = X
+            run = lambda: D.lu_distributed(A, block_size=256)  # noqa: E731
+        del X
+        times = []
+        for _ in range(2):
+            dist.barrier(device_ids=[dev.index])
+            torch.cuda.synchronize(dev)
+            t0 = time.perf_counter()
+            out = run()
+            torch.cuda.synchronize(dev)
+            times.append(time.perf_counter() - t0)
+        t = torch.tensor([times[-1]], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        if rank == 0:
+            if args.workload == "cholesky":
+                same = torch.equal(out.view(torch.int64), ti.cholesky(A, block_size=256).view(torch.int64))
+                err = (torch.linalg.norm(A - out @ out.T) / torch.linalg.norm(A)).item()
+            else:
+                one = ti.lu(A, block_size=256)
+                same = all(torch.equal(a.view(torch.int64), b.view(torch.int64))
+                           for a, b in zip(out, one))
+                P, L, U = out
+                err = (torch.linalg.norm(P @ A - L @ U) / torch.linalg.norm(A)).item()
+            line.update({"n": n, "block": 256, "n_gpus": world,
+                         "layout": "block-cyclic columns, panel broadcast over NCCL",
+                         "seconds": float(t.item()), "backward_error_fro": err,
+                         "bit_identical_to_one_gpu": bool(same)})
+            print(json.dumps(line), flush=True)
+        dist.barrier(device_ids=[dev.index])
+    finally:
+        dist.destroy_process_group()
 
 
 def main():
