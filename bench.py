@@ -41,10 +41,10 @@ METRIC = "emulated FP64 GEMM TFLOP/s at 8192³, 1/2/4/8 B200; % of int8 TC peak"
 UNIT = "TFLOP/s"
 GRIDS = {1: (1, 1), 2: (1, 2), 4: (2, 2), 8: (2, 4)}
 # dram__bytes_read.sum + dram__bytes_write.sum of one residue-GEMM launch (the CTA-pair kernel)
-# at 8192^3 with the 16 wide moduli: the mean of three launches (6.59 GB read + 1.06 GB
-# written each), from the 1-pass ncu launch list summarised in
-# profiles/launches_crt_matmul_8192.md.
-GEMM_DRAM_BYTES_8192 = 7657961813
+# at 8192^3 with the 16 wide moduli: the mean of three launches (5.12 GB read + 1.06 GB
+# written), from the 1-pass ncu launch list summarised in profiles/launches_crt_matmul_8192.md
+# (another box gave 6.59 + 1.06 GB: the re-reads of B depend on how the pairs drift apart).
+GEMM_DRAM_BYTES_8192 = 6186950229
 
 
 def parse_args():
@@ -417,6 +417,24 @@ def run_ours(args):
         prim = {"n_moduli": n_mod_primes, "ms_per_step": ms_p, "steps": steps_p,
                 "value": world * flops / (ms_p * 1e-3) / 1e12}
 
+    # cuBLAS DGEMM (torch.matmul float64) on the same operands, for context (rank 0 only)
+    dgemm = None
+    if rank == 0:
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                torch.matmul(A, B)
+            d0 = torch.cuda.Event(enable_timing=True)
+            d1 = torch.cuda.Event(enable_timing=True)
+            d0.record(stream)
+            for _ in range(3):
+                torch.matmul(A, B)
+            d1.record(stream)
+        d1.synchronize()
+        ms_d = d0.elapsed_time(d1) / 3
+        dgemm = {"cublas_dgemm_ms": ms_d, "cublas_dgemm_tflops": flops / (ms_d * 1e-3) / 1e12,
+                 "note": "torch.matmul float64 on the same device-resident operands, 3 calls "
+                         "after 2 warm-up calls; context only"}
+
     Ah = A.cpu().pin_memory()
     Bh = B.cpu().pin_memory()
     # warm-up holds each result while the next call allocates its own, as the timed loop
@@ -533,7 +551,7 @@ def run_ours(args):
                        "parallelism": f"output blocks over {world} GPU(s), no collective"},
             "e2e": e2e, "roofline": roof, "cpu_baseline": cpu, "clocks": clocks,
             "gpu_launches": 6 * args.steps, "stages": stages, "spot_check_bitexact": spot_ok,
-            "accuracy": accuracy, "reference_moduli": prim,
+            "accuracy": accuracy, "reference_moduli": prim, "context_fp64": dgemm,
         }
         print(json.dumps(line), flush=True)
     if dist is not None:

@@ -144,6 +144,68 @@ __global__ void exp_cols_kernel(const double *__restrict__ X, int64_t outer, int
     }
 }
 
+// Outer contiguous, long vectors: two passes.  Block (g, s) takes 64 consecutive vectors
+// (each lane two neighbours, one 16-byte load per k) over the s-th of kExpColSplit slices
+// of k, 8 warps striding the slice with 4 loads in flight each, and writes the slice's
+// maximum bit patterns to part[s][o]; exp_cols_finish_kernel reduces the slices.  The
+// one-pass kernel above gives only outer / 32 blocks of 1024 threads (256 at outer = 8192,
+// fewer than two per SM) with 8-byte loads.
+constexpr int kExpColSplit = 8;
+
+__global__ void __launch_bounds__(256)
+    exp_cols_partial_kernel(const double *__restrict__ X, int64_t outer, int64_t kdim,
+                            int64_t s_k, uint64_t *__restrict__ part) {
+    __shared__ uint64_t red[8][64];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t o = int64_t(blockIdx.x) * 64 + 2 * lane;
+    const int64_t per = (kdim + kExpColSplit - 1) / kExpColSplit;
+    const int64_t l0 = int64_t(blockIdx.y) * per;
+    const int64_t l1 = l0 + per < kdim ? l0 + per : kdim;
+    uint64_t m0 = 0, m1 = 0;
+    if (o + 1 < outer) {
+        int64_t l = l0 + warp;
+        for (; l + 24 < l1; l += 32) {
+            double2 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                v[u] = __ldg(reinterpret_cast<const double2 *>(X + (l + 8 * u) * s_k + o));
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                m0 = max(m0, abs_bits(v[u].x));
+                m1 = max(m1, abs_bits(v[u].y));
+            }
+        }
+        for (; l < l1; l += 8) {
+            const double2 v = __ldg(reinterpret_cast<const double2 *>(X + l * s_k + o));
+            m0 = max(m0, abs_bits(v.x));
+            m1 = max(m1, abs_bits(v.y));
+        }
+    } else if (o < outer) {  // the last vector when outer is odd
+        for (int64_t l = l0 + warp; l < l1; l += 8) m0 = max(m0, abs_bits(__ldg(X + l * s_k + o)));
+    }
+    red[warp][2 * lane] = m0;
+    red[warp][2 * lane + 1] = m1;
+    __syncthreads();
+    if (threadIdx.x < 64) {
+        uint64_t m = red[0][threadIdx.x];
+#pragma unroll
+        for (int w = 1; w < 8; ++w) m = max(m, red[w][threadIdx.x]);
+        const int64_t oc = int64_t(blockIdx.x) * 64 + threadIdx.x;
+        if (oc < outer) part[int64_t(blockIdx.y) * outer + oc] = m;
+    }
+}
+
+__global__ void exp_cols_finish_kernel(const uint64_t *__restrict__ part, int64_t outer,
+                                       int32_t *__restrict__ exp_out) {
+    for (int64_t o = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; o < outer;
+         o += int64_t(gridDim.x) * blockDim.x) {
+        uint64_t m = part[o];
+#pragma unroll
+        for (int s = 1; s < kExpColSplit; ++s) m = max(m, part[int64_t(s) * outer + o]);
+        exp_out[o] = exp_from_maxbits(m);
+    }
+}
+
 // ---------------------------------------------------------------------------------------
 // pass 2: scale + residues
 // ---------------------------------------------------------------------------------------
@@ -305,9 +367,24 @@ cudaError_t launch_split(const double *X, int64_t outer, int64_t kdim, int64_t s
                                                                res, ld_res, plane, C);
     } else {
         const int64_t blocks = (outer + 31) / 32;
-        if (!exps_given)
+        // two passes for long vectors, their partial maxima parked in the first residue plane
+        // (kExpColSplit * outer * 8 bytes <= outer * ld_res; the split overwrites it next)
+        const bool two_pass = kdim >= 1024 && ld_res >= 8 * kExpColSplit &&
+                              (reinterpret_cast<uintptr_t>(X) & 15) == 0 && (s_k & 1) == 0 &&
+                              (reinterpret_cast<uintptr_t>(res) & 7) == 0 &&
+                              (outer + 63) / 64 <= 65535 * 1024;
+        if (!exps_given && two_pass) {
+            uint64_t *part = reinterpret_cast<uint64_t *>(res);
+            exp_cols_partial_kernel<<<dim3(static_cast<unsigned>((outer + 63) / 64), kExpColSplit),
+                                      256, 0, stream>>>(X, outer, kdim, s_k, part);
+            int64_t fb = (outer + 255) / 256;
+            if (fb > int64_t(num_sms) * 8) fb = int64_t(num_sms) * 8;
+            exp_cols_finish_kernel<<<static_cast<unsigned>(fb), 256, 0, stream>>>(part, outer,
+                                                                                 exp_out);
+        } else if (!exps_given) {
             exp_cols_kernel<<<static_cast<unsigned>(blocks), 1024, 0, stream>>>(X, outer, kdim,
                                                                                 s_k, exp_out);
+        }
         if (try_tc) {
             const cudaError_t e = launch_split_tc(X, outer, kdim, 1, s_k, C, exp_out, res,
                                                   ld_res, plane, err, tc_ctas, stream);

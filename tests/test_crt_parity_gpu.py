@@ -178,12 +178,14 @@ def test_update_on_submatrix_view(ti, oracle):
     _assert_bitexact(Wd, want)
 
 
-def test_nonfinite_rows_and_cols(ti, oracle):
-    A = _rand((40, 60), 51)
-    B = _rand((60, 30), 52)
+@pytest.mark.parametrize("k", [60, 1100])  # 1100: the two-pass column exponents
+def test_nonfinite_rows_and_cols(ti, oracle, k):
+    A = _rand((40, k), 51)
+    B = _rand((k, 30), 52)
     A[3, 7] = float("nan")
     A[9, 0] = float("inf")
     B[5, 11] = float("-inf")
+    B[k - 1, 20] = 1e300  # a large entry in the last slice of k
     C = ti.crt_matmul(A.cuda(), B.cuda()).cpu()
     assert torch.isnan(C[3]).all() and torch.isnan(C[9]).all() and torch.isnan(C[:, 11]).all()
     keep_r = [i for i in range(40) if i not in (3, 9)]
