@@ -454,15 +454,27 @@ def cholesky_cyclic(A_local, n: int, block_size: int = 64, *, group=None, matmul
         bw = min(b, n - j)
         jb = j + bw
         owner = c % world
+        failure = None
         if rank == owner:
             lc = local_off[c]
-            # panel: small Cholesky on the diagonal block (cholesky.py:24)
-            L[j:jb, lc:lc + bw] = torch.linalg.cholesky(W[j:jb, lc:lc + bw])
-            if jb < n:
-                # triangular solve for the sub-diagonal block (cholesky.py:28-30)
-                L[jb:, lc:lc + bw] = torch.linalg.solve_triangular(
-                    L[j:jb, lc:lc + bw], W[jb:, lc:lc + bw].T, upper=False
-                ).T
+            try:
+                # panel: small Cholesky on the diagonal block (cholesky.py:24)
+                L[j:jb, lc:lc + bw] = torch.linalg.cholesky(W[j:jb, lc:lc + bw])
+                if jb < n:
+                    # triangular solve for the sub-diagonal block (cholesky.py:28-30)
+                    L[jb:, lc:lc + bw] = torch.linalg.solve_triangular(
+                        L[j:jb, lc:lc + bw], W[jb:, lc:lc + bw].T, upper=False
+                    ).T
+            except RuntimeError as e:  # not positive definite: every rank must learn of it
+                failure = e
+        if world > 1:
+            flag = torch.tensor([1 if failure is not None else 0], device=dev)
+            dist.broadcast(flag, src=_global_rank(group, owner), group=group)
+            if int(flag.item()) and failure is None:
+                raise RuntimeError(f"cholesky_distributed: the panel at column {j} failed on "
+                                   f"rank {owner} (matrix not positive definite?)")
+        if failure is not None:
+            raise failure
         if jb >= n:
             break
         if rank == owner:

@@ -122,3 +122,37 @@ def _gpu_worker(rank, world, port, kind, n, block):
                                           ("spd", 650, 64), ("randn", 1300, 256)])
 def test_cyclic_factorizations_gpu_match_one_gpu(kind, n, block):
     mp.spawn(_gpu_worker, args=(2, _free_port(), kind, n, block), nprocs=2, join=True)
+
+
+def _cpu_fail_worker(rank, world, port, errs):
+    import torch.distributed as dist
+
+    from tensor_inv_b200 import distributed as D
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        A = -torch.eye(24, dtype=torch.float64)  # not positive definite
+        try:
+            D.cholesky_distributed(A, 8, matmul=lambda a, b: a @ b)
+            errs.put(f"rank {rank}: no error raised")
+        except RuntimeError:
+            pass
+    finally:
+        dist.destroy_process_group()
+
+
+def test_cyclic_cholesky_failure_reaches_every_rank():
+    """A panel that fails on its owner raises on every rank instead of leaving the others
+    waiting in the next broadcast."""
+    ctx = mp.get_context("spawn")
+    errs = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_cpu_fail_worker, args=(r, 2, port, errs)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert errs.empty(), errs.get()
