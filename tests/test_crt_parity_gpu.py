@@ -573,6 +573,16 @@ def test_host_pipeline_uneven_bands(ti, b_colmajor):
     _assert_bitexact(C, want.cpu().numpy())
 
 
+def test_host_pipeline_bands_on_pair_gemm(ti):
+    """Uneven host bands with K >= 1024 and n >= 256: each band's GEMM runs on CTA pairs."""
+    m, n, k = 4100, 300, 1100
+    A = _rand((m, k), 175, 1.0).pin_memory()
+    B = _rand((k, n), 176, 1.0).pin_memory()
+    C = ti.crt_matmul(A, B, moduli="wide")
+    want = ti.crt_matmul(A.cuda(), B.cuda(), moduli="wide")
+    _assert_bitexact(C, want.cpu().numpy())
+
+
 def test_host_pipeline_transposed_views(ti, oracle):
     A = _rand((300, 900), 141, 0.5).T     # 900 x 300, column-major view
     B = _rand((250, 300), 142, 0.5).T     # 300 x 250, column-major view
