@@ -565,6 +565,18 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def rsvd_matrix(torch, m, n, r, dev):
+    """A = U diag(0.95^i) V^T + 1e-8 N(0,1), rank r, seeded on the device (the same on every
+    device)."""
+    g = torch.Generator(device=dev).manual_seed(0)
+    Uq, _ = torch.linalg.qr(torch.randn(m, r, generator=g, dtype=torch.float64, device=dev))
+    Vq, _ = torch.linalg.qr(torch.randn(n, r, generator=g, dtype=torch.float64, device=dev))
+    sig = 0.95 ** torch.arange(r, dtype=torch.float64, device=dev)
+    A = (Uq * sig) @ Vq.T + 1e-8 * torch.randn(m, n, generator=g, dtype=torch.float64,
+                                                device=dev)
+    return A, sig
+
+
 def run_factorization(args):
     """LU / Cholesky / randomized SVD with every trailing-update or projection GEMM on the CRT
     kernels, timed end to end on one GPU (second of two calls of the same size), with the
@@ -591,8 +603,6 @@ def run_factorization(args):
             "device": torch.cuda.get_device_name(dev)}
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if world > 1:
-        if args.workload not in ("lu", "cholesky"):
-            raise SystemExit("--workload rsvd runs on one GPU (rsvd_rows is tested, not timed)")
         return run_factorization_cyclic(args, dev, line, world)
     if args.workload == "lu":
         n = args.order or 16384
@@ -617,11 +627,7 @@ def run_factorization(args):
     else:
         m = args.order or 65536
         n, r = 8192, 256
-        Uq, _ = torch.linalg.qr(torch.randn(m, r, generator=g, dtype=torch.float64, device=dev))
-        Vq, _ = torch.linalg.qr(torch.randn(n, r, generator=g, dtype=torch.float64, device=dev))
-        sig = 0.95 ** torch.arange(r, dtype=torch.float64, device=dev)
-        A = (Uq * sig) @ Vq.T + 1e-8 * torch.randn(m, n, generator=g, dtype=torch.float64,
-                                                    device=dev)
+        A, sig = rsvd_matrix(torch, m, n, r, dev)
         torch.manual_seed(1)
         (U, S, Vt), t = timed(lambda: ti.rsvd(A, rank=r, n_oversamples=10, n_power_iter=2))
         err = (torch.linalg.norm(A - (U * S) @ Vt) / torch.linalg.norm(A)).item()
@@ -632,10 +638,10 @@ def run_factorization(args):
 
 
 def run_factorization_cyclic(args, dev, line, world):
-    """Block-cyclic LU / Cholesky over the ranks (tensor_inv_b200.distributed): every rank
-    builds the same matrix, the factorisation is timed with a barrier and a device sync on both
-    sides (second of two calls, max over ranks), and rank 0 checks the gathered factors bit for
-    bit against the one-GPU routine."""
+    """Block-cyclic LU / Cholesky, or rSVD with A's rows sharded, over the ranks
+    (tensor_inv_b200.distributed): every rank builds the same matrix, the routine is timed with
+    a barrier and a device sync on both sides (second of two calls, max over ranks), and rank 0
+    checks its results bit for bit against the one-GPU routine."""
     import datetime
 
     import torch
@@ -647,16 +653,26 @@ def run_factorization_cyclic(args, dev, line, world):
     dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=180))
     rank = dist.get_rank()
     try:
-        n = args.order or 16384
-        g = torch.Generator(device=dev).manual_seed(0)
-        X = torch.randn(n, n, generator=g, dtype=torch.float64, device=dev)
-        if args.workload == "cholesky":
-            A = X @ X.T / n + 1e-6 * torch.eye(n, dtype=torch.float64, device=dev)
-            run = lambda: D.cholesky_distributed(A, block_size=256)  # noqa: E731
+        if args.workload == "rsvd":
+            n = args.order or 65536
+            ncols, r = 8192, 256
+            A, sig = rsvd_matrix(torch, n, ncols, r, dev)
+            r0, r1 = D.block_range(n, world, rank)
+
+            def run():
+                torch.manual_seed(1)  # the same Omega on every rank, as on one GPU
+                return D.rsvd_rows(A[r0:r1], rank=r, n_oversamples=10, n_power_iter=2)
         else:
-            A = X
-            run = lambda: D.lu_distributed(A, block_size=256)  # noqa: E731
-        del X
+            n = args.order or 16384
+            g = torch.Generator(device=dev).manual_seed(0)
+            X = torch.randn(n, n, generator=g, dtype=torch.float64, device=dev)
+            if args.workload == "cholesky":
+                A = X @ X.T / n + 1e-6 * torch.eye(n, dtype=torch.float64, device=dev)
+                run = lambda: D.cholesky_distributed(A, block_size=256)  # noqa: E731
+            else:
+                A = X
+                run = lambda: D.lu_distributed(A, block_size=256)  # noqa: E731
+            del X
         times = []
         for _ in range(2):
             dist.barrier(device_ids=[dev.index])
@@ -667,7 +683,22 @@ def run_factorization_cyclic(args, dev, line, world):
             times.append(time.perf_counter() - t0)
         t = torch.tensor([times[-1]], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        if rank == 0:
+        if rank == 0 and args.workload == "rsvd":
+            torch.manual_seed(1)
+            U1, S1, Vt1 = ti.rsvd(A, rank=r, n_oversamples=10, n_power_iter=2)
+            U, S, Vt = out
+            same = (torch.equal(S.view(torch.int64), S1.view(torch.int64))
+                    and torch.equal(Vt.view(torch.int64), Vt1.view(torch.int64))
+                    and torch.equal(U.view(torch.int64), U1[r0:r1].view(torch.int64)))
+            line.update({"m": n, "n": ncols, "rank": r, "oversampling": 10,
+                         "power_iterations": 2, "n_gpus": world,
+                         "layout": "rows of A sharded; A^T Q and Q^T A through the exact "
+                                   "int32 residue all-reduce",
+                         "seconds": float(t.item()),
+                         "max_singular_value_error": ((S - sig).abs().max() / sig[0]).item(),
+                         "bit_identical_to_one_gpu": bool(same)})
+            print(json.dumps(line), flush=True)
+        elif rank == 0:
             if args.workload == "cholesky":
                 same = torch.equal(out.view(torch.int64), ti.cholesky(A, block_size=256).view(torch.int64))
                 err = (torch.linalg.norm(A - out @ out.T) / torch.linalg.norm(A)).item()
