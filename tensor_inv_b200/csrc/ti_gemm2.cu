@@ -51,10 +51,9 @@ struct PairParams {
     int64_t total_units;
     void *out;
     int64_t ldo, plane;
-    int out_i32, store_t, lower;
+    int out_i32, lower;
     uint32_t idesc;
     ModMagic mm;
-    uint32_t u[kMaxModuli];
     int *err;
 };
 
@@ -330,16 +329,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
                     // nothing to store for this lane and chunk
                 } else if (!P.out_i32) {
                     uint32_t pk[8];
-                    const uint32_t wt = P.store_t ? P.u[mod] : 1u;
 #pragma unroll
                     for (int j = 0; j < 8; ++j) {
                         uint32_t w = 0;
 #pragma unroll
-                        for (int b = 0; b < 4; ++b) {
-                            uint32_t r = mod_acc(v[4 * j + b], p, magic, shift, off);
-                            if (P.store_t) r = mod_small(r * wt, p, magic, shift);
-                            w |= r << (8 * b);
-                        }
+                        for (int b = 0; b < 4; ++b)
+                            w |= mod_acc(v[4 * j + b], p, magic, shift, off) << (8 * b);
                         pk[j] = w;
                     }
                     uint8_t *dst = static_cast<uint8_t *>(P.out) + mod * P.plane + row * P.ldo + col0;
@@ -410,7 +405,8 @@ static int pair_capacity(int dev) {
 
 // The pair kernel for R[i] = (A_i @ B_i^T) mod p_i (same arguments and output as
 // launch_residue_gemm's unfused mode).  Returns cudaErrorNotSupported when the device cannot
-// run CTA pairs (the caller then uses the one-CTA kernel).
+// run CTA pairs or when output weights are asked for (the caller then uses the one-CTA
+// kernel, which also writes (r_i * weights[i]) mod p_i).
 cudaError_t launch_residue_gemm_pair(const int8_t *a_res, const int8_t *b_res, int64_t m,
                                      int64_t n, int64_t kdim, int64_t ld, int n_mod,
                                      const ModMagic &mm, void *out, int64_t ldo, int out_i32,
@@ -419,6 +415,7 @@ cudaError_t launch_residue_gemm_pair(const int8_t *a_res, const int8_t *b_res, i
                                      bool unsigned_ops, bool lower) {
     if (m == 0 || n == 0 || n_mod == 0) return cudaSuccess;
     if (kdim <= 0) return cudaErrorInvalidValue;
+    if (weights && !out_i32) return cudaErrorNotSupported;
     int dev = 0;
     cudaGetDevice(&dev);
     const int pairs_max = pair_capacity(dev);
@@ -444,10 +441,6 @@ cudaError_t launch_residue_gemm_pair(const int8_t *a_res, const int8_t *b_res, i
     P.idesc = unsigned_ops ? make_idesc_u8(kPM, kPN) : make_idesc_i8(kPM, kPN);
     P.mm = mm;
     P.err = err;
-    if (weights && !out_i32) {
-        P.store_t = 1;
-        for (int i = 0; i < n_mod; ++i) P.u[i] = weights[i];
-    }
     const int64_t pairs = P.total_units < pairs_max ? P.total_units : pairs_max;
     residue_gemm_pair_kernel<<<static_cast<unsigned>(2 * pairs), kPThreads, kPSmemBytes, stream>>>(
         tmA, tmB, P);
