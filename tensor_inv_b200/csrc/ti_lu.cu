@@ -455,17 +455,27 @@ int ti_lu_panel_ex(double *W, int64_t ldw, int64_t n, int64_t ncols, int64_t j, 
     if (g_smem > kLuSmemMaxCtas) g_smem = kLuSmemMaxCtas;
     const int64_t per = (n - j + g_smem - 1) / g_smem;
     const size_t smem = lu_smem_bytes(per, b);
-    if (b <= kLuSmemMaxPanel && smem <= size_t(200) * 1024) {
-        static int configured = -1;
-        int dev = 0;
-        cudaGetDevice(&dev);
-        if (configured != dev) {
-            if (cudaFuncSetAttribute(lu_panel_smem_kernel,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     200 * 1024) != cudaSuccess)
-                return TI_ERR_CUDA;
-            configured = dev;
-        }
+    // the largest dynamic shared memory a CTA may take: the opt-in limit less the kernel's
+    // static arrays (at b = 256 this holds 111 rows per CTA: n = 16384 on 148 SMs)
+    static int configured = -1;
+    static size_t max_dyn = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (configured != dev) {
+        cudaFuncAttributes fa;
+        int optin = 0;
+        if (cudaFuncGetAttributes(&fa, lu_panel_smem_kernel) != cudaSuccess ||
+            cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) !=
+                cudaSuccess ||
+            optin <= static_cast<int>(fa.sharedSizeBytes))
+            return TI_ERR_CUDA;
+        max_dyn = size_t(optin) - fa.sharedSizeBytes;
+        if (cudaFuncSetAttribute(lu_panel_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(max_dyn)) != cudaSuccess)
+            return TI_ERR_CUDA;
+        configured = dev;
+    }
+    if (b <= kLuSmemMaxPanel && smem <= max_dyn) {
         int per_sm_s = 0;
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_s, lu_panel_smem_kernel,
                                                           kLuThreads, smem) == cudaSuccess &&
