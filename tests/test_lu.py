@@ -90,6 +90,7 @@ def test_device_panel_edge_sizes(monkeypatch, n, block):
 @pytest.mark.parametrize("n,ncols,j,b,pc", [
     (700, 380, 0, 64, 0), (700, 380, 128, 64, 64), (700, 380, 640, 60, 320),
     (300, 500, 40, 64, 300), (900, 600, 100, 300, 150),   # b > 256: the global-memory kernel
+    (16384, 400, 0, 256, 100),  # 111 rows of 256 columns per CTA: ~223 KB of shared memory
 ])
 def test_panel_at_shifted_columns(n, ncols, j, b, pc):
     """ti_lu_panel_ex: the panel of rows [j, n) in columns [pc, pc + b) of a rectangular W,
