@@ -369,16 +369,22 @@ __global__ void __launch_bounds__(kLuThreads)
         }
         __syncthreads();
 
-        // ---- C: scale and update owned rows > k in shared memory
+        // ---- C: scale and update owned rows > k in shared memory: first every row's
+        // multiplier l = W[i, k] / d, one row per thread (the divisions in parallel), then the
+        // rank-1 update of the row's later panel columns, a warp per row
         const double d = urow[kc];
         if (fabs(d) > 1e-15) {
-            for (int64_t i = (r0 > k + 1 ? r0 : k + 1) + warp; i < r1; i += kLuThreads / 32) {
+            const int64_t i0 = r0 > k + 1 ? r0 : k + 1;
+            for (int64_t i = i0 + tid; i < r1; i += kLuThreads) {
                 double *pi = P + (i - r0) * pitch;
-                const double l = __ddiv_rn(pi[kc], d);
+                pi[kc] = __ddiv_rn(pi[kc], d);
+            }
+            __syncthreads();
+            for (int64_t i = i0 + warp; i < r1; i += kLuThreads / 32) {
+                double *pi = P + (i - r0) * pitch;
+                const double l = pi[kc];
                 for (int c = kc + 1 + lane; c < b; c += 32)
                     pi[c] = __dsub_rn(pi[c], __dmul_rn(l, urow[c]));
-                __syncwarp();
-                if (lane == 0) pi[kc] = l;
             }
         }
         __syncthreads();
