@@ -65,6 +65,16 @@ struct GemmParams {
     uint32_t idesc;    // MMA instruction descriptor: signed or unsigned 8-bit operands
     int lower;         // unfused: skip output tiles entirely above the diagonal
     int epi_warps;     // 8 when the K loop is short (the epilogue bounds the tile), else 4
+    // |accumulator| < 2^22 - 256 (short K loops): r = acc mod p from a rounded float32
+    // quotient of T = acc + qofs[i] (0 <= T < 2^23): q = round(T / p) from
+    // fma(T * 2^-49, qinv[i], qmagic[i]) (T read as the subnormal T * 2^-149, times 2^100;
+    // qinv = 2^49 / p correctly rounded, so the quotient is exact for T < 2^23), and
+    // r = T - p * bits(q) (mod 2^8), qmagic = 1.5 * 2^23 + kappa with p * kappa == -h
+    // (mod 2^8) so the byte is (acc + qofs + h) - p * q = acc mod p, h = (p - 1) / 2.
+    int small_acc;
+    uint32_t qofs[kMaxModuli];
+    float qinv[kMaxModuli];
+    float qmagic[kMaxModuli];
     // fused output
     uint8_t *scratch;  // 2 slots x n_mod x 128 x 256 bytes per CTA
     const int32_t *row_exp, *col_exp;
@@ -396,6 +406,28 @@ __global__ void __launch_bounds__(gemm_threads(kFused), 1)
                                 }
                                 pk[j] = w;
                             }
+                        } else if (P.small_acc) {  // r itself, float32 quotient (see GemmParams)
+                            const uint32_t qofs = P.qofs[mod], negp = 0u - p;
+                            const float2 qinv = make_float2(P.qinv[mod], P.qinv[mod]);
+                            const float2 qmag = make_float2(P.qmagic[mod], P.qmagic[mod]);
+                            const float2 two100 = make_float2(0x1p100f, 0x1p100f);
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) {
+                                uint32_t r[4];
+#pragma unroll
+                                for (int b = 0; b < 4; b += 2) {
+                                    const uint32_t t0 = v[4 * j + b] + qofs;
+                                    const uint32_t t1 = v[4 * j + b + 1] + qofs;
+                                    const float2 q = __ffma2_rn(
+                                        __fmul2_rn(make_float2(__uint_as_float(t0),
+                                                               __uint_as_float(t1)), two100),
+                                        qinv, qmag);
+                                    r[b] = t0 + negp * __float_as_uint(q.x);  // low byte
+                                    r[b + 1] = t1 + negp * __float_as_uint(q.y);
+                                }
+                                pk[j] = __byte_perm(__byte_perm(r[0], r[1], 0x0040),
+                                                    __byte_perm(r[2], r[3], 0x0040), 0x5410);
+                            }
                         } else {  // r itself (the matmul path folds u into A's residues)
 #pragma unroll
                             for (int j = 0; j < 8; ++j) {
@@ -529,6 +561,21 @@ static cudaError_t fill_common(GemmParams &P, CUtensorMap &tmA, CUtensorMap &tmB
     P.mm = mm;
     P.err = err;
     P.idesc = unsigned_ops ? make_idesc_u8(kBM, kBN) : kIdesc;
+    // the float32 quotient when every accumulator is below 2^22 - 256 in magnitude
+    const int64_t amax = unsigned_ops ? 254 : 127;
+    if (kdim * amax * amax < (int64_t(1) << 22) - 256) {
+        P.small_acc = 1;
+        for (int i = 0; i < n_mod; ++i) {
+            const uint32_t p = mm.p[i], h = (p - 1) / 2;
+            const uint32_t off = p * (((uint32_t(1) << 22) + p - 1) / p);  // multiple of p >= 2^22
+            P.qofs[i] = off - h;
+            P.qinv[i] = 562949953421312.0f / static_cast<float>(p);  // 2^49 / p, rounded once
+            uint32_t pinv8 = 1;  // p^-1 mod 2^8 (p odd): Newton steps double the correct bits
+            for (int it = 0; it < 4; ++it) pinv8 *= 2u - p * pinv8;
+            const uint32_t kappa = ((256u - (h & 255u)) * pinv8) & 255u;  // p * kappa == -h
+            P.qmagic[i] = 12582912.0f + static_cast<float>(kappa);       // 1.5 * 2^23 + kappa
+        }
+    }
     return P.num_kb > 0 ? cudaSuccess : cudaErrorInvalidValue;
 }
 
