@@ -55,20 +55,39 @@ __device__ __forceinline__ bool lu_better(double av, long long ai, double bv, lo
 
 // Grid-wide barrier over `nblocks` co-resident CTAs.  Returns false (in every thread of the
 // CTA) if a wait ran out or another CTA gave up.
+__device__ __forceinline__ unsigned lu_atom_add_acq_rel(unsigned *p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+__device__ __forceinline__ unsigned lu_ld_acquire(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void lu_st_release(unsigned *p, unsigned v) {
+    asm volatile("st.release.gpu.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Grid-wide barrier over `nblocks` co-resident CTAs.  Returns false (in every thread of the
+// CTA) if a wait ran out or another CTA gave up.  Thread 0 arrives with an acquire-release
+// add on the counter (after the CTA barrier, so it carries the CTA's writes); the last
+// arrival resets the counter and releases the generation word, which the others poll with
+// acquire loads.
 __device__ bool lu_grid_sync(LuSync *s, unsigned nblocks, unsigned &gen_local, int *err) {
     __shared__ int ok_sh;
     __syncthreads();
     if (threadIdx.x == 0) {
         int ok = 1;
         const unsigned target = gen_local + 1;
-        __threadfence();  // this CTA's writes before its arrival
-        if (atomicAdd(&s->count, 1u) == nblocks - 1) {
-            atomicExch(&s->count, 0u);
-            __threadfence();
-            atomicExch(&s->gen, target);  // release everyone
+        if (lu_atom_add_acq_rel(&s->count, 1u) == nblocks - 1) {
+            s->count = 0u;  // ordered before the release below
+            lu_st_release(&s->gen, target);
         } else {
             const unsigned long long t0 = globaltimer_ns();
-            while (*reinterpret_cast<volatile unsigned *>(&s->gen) != target) {
+            while (lu_ld_acquire(&s->gen) != target) {
                 if (*reinterpret_cast<volatile int *>(&s->abort)) {
                     ok = 0;
                     break;
@@ -79,10 +98,8 @@ __device__ bool lu_grid_sync(LuSync *s, unsigned nblocks, unsigned &gen_local, i
                     ok = 0;
                     break;
                 }
-                __nanosleep(64);
             }
         }
-        __threadfence();  // the other CTAs' writes after the release
         gen_local = target;
         ok_sh = ok;
     }
