@@ -107,6 +107,43 @@ __device__ bool lu_grid_sync(LuSync *s, unsigned nblocks, unsigned &gen_local, i
     return ok_sh != 0;
 }
 
+// lu_grid_sync in two halves, so a CTA can work between its arrival and its wait.
+// lu_grid_arrive: called by every thread after the CTA's writes that the other CTAs read.
+__device__ __forceinline__ void lu_grid_arrive(LuSync *s, unsigned nblocks, unsigned &gen_local) {
+    __syncthreads();
+    const unsigned target = gen_local + 1;
+    if (threadIdx.x == 0 && lu_atom_add_acq_rel(&s->count, 1u) == nblocks - 1) {
+        s->count = 0u;  // ordered before the release below
+        lu_st_release(&s->gen, target);
+    }
+    gen_local = target;
+}
+
+// lu_grid_wait: until every CTA has arrived at generation gen_local (bounded; false in every
+// thread if the wait ran out or another CTA gave up).  Ends with a CTA barrier.
+__device__ bool lu_grid_wait(LuSync *s, unsigned gen_local, int *err) {
+    __shared__ int ok_sh;
+    if (threadIdx.x == 0) {
+        int ok = 1;
+        const unsigned long long t0 = globaltimer_ns();
+        while (lu_ld_acquire(&s->gen) != gen_local) {
+            if (*reinterpret_cast<volatile int *>(&s->abort)) {
+                ok = 0;
+                break;
+            }
+            if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+                atomicExch(&s->abort, 1);
+                atomicCAS(err, 0, kErrTimeoutGridBarrier);
+                ok = 0;
+                break;
+            }
+        }
+        ok_sh = ok;
+    }
+    __syncthreads();
+    return ok_sh != 0;
+}
+
 // The global pivot from the G published candidates: thread t loads candidate t (all loads in
 // flight at once), then a warp and a block reduction.  Every CTA reduces the same values with
 // the same total order (value, then index), so all CTAs agree.  Returns the row in *row and the
@@ -264,13 +301,19 @@ __global__ void __launch_bounds__(kLuThreads)
 // ---------------------------------------------------------------------------------------
 // Shared-memory variant: each CTA keeps its panel rows (all b columns) in shared memory for
 // the whole panel, so the column updates never touch global memory, and one grid barrier per
-// column suffices.  Before the barrier every CTA publishes its argmax candidate and that
-// candidate's panel row, and the owner of row k publishes row k (double-buffered by column
-// parity: a CTA can only write column k+1's slots after every CTA has passed column k's
+// column suffices.  Before column k's barrier every CTA publishes its argmax candidate and
+// that candidate's panel row, and the owner of row k publishes row k (double-buffered by
+// column parity: a CTA can only write column k+1's slots after every CTA has passed column k's
 // barrier, and it reads column k's slots before arriving at column k+1's).  After the barrier
 // every CTA takes the pivot row from the winner's slot; the owners of rows k and p swap their
-// panel parts from the slots, and the columns outside the panel are swapped in global memory
-// (each CTA always takes the same column slice, so its swaps stay in program order).
+// panel parts from the slots.
+// The barrier is split into an arrival and a wait, and column k+1's candidate is found ahead
+// of the rest of column k's update: each CTA divides its rows' multipliers and updates
+// column k+1 only, takes its candidate for column k+1, finishes the two rows it may publish
+// (the candidate and row k+1), publishes and arrives; the rest of the rank-1 update
+// (columns k+2 ..) and the swap of the columns outside the panel (in global memory, each
+// CTA always on the same column slice, so its swaps stay in program order) run while the
+// other CTAs arrive.  Every element receives the same operations in the same order.
 // ---------------------------------------------------------------------------------------
 constexpr int kLuSmemMaxPanel = 256;
 constexpr int kLuSmemMaxCtas = 256;
@@ -280,6 +323,66 @@ struct LuSlots {
     double krow[2][kLuSmemMaxPanel];
     double crow[2][kLuSmemMaxCtas][kLuSmemMaxPanel];
 };
+
+// This CTA's argmax candidate for column k (panel column kc of P) over its rows >= k.  Thread 0
+// writes it to *slot and to *best (shared); every thread returns it.
+__device__ __forceinline__ long long lu_cta_candidate(const double *P, int pitch, int64_t r0,
+                                                      int64_t r1, int64_t k, int kc,
+                                                      double *red_v, long long *red_i,
+                                                      LuCand *slot, long long *best) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    double bv = -1.0;
+    long long bi = LLONG_MAX;
+    for (int64_t i = (r0 > k ? r0 : k) + tid; i < r1; i += kLuThreads) {
+        const double v = fabs(P[(i - r0) * pitch + kc]);
+        if (bi == LLONG_MAX || lu_better(v, i, bv, bi)) {
+            bv = v;
+            bi = i;
+        }
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) {
+        const double ov = __shfl_xor_sync(0xFFFFFFFFu, bv, off);
+        const long long oi = __shfl_xor_sync(0xFFFFFFFFu, bi, off);
+        if (oi != LLONG_MAX && (bi == LLONG_MAX || lu_better(ov, oi, bv, bi))) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    if (lane == 0) {
+        red_v[warp] = bv;
+        red_i[warp] = bi;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        for (int w = 1; w < kLuThreads / 32; ++w)
+            if (red_i[w] != LLONG_MAX &&
+                (bi == LLONG_MAX || lu_better(red_v[w], red_i[w], bv, bi))) {
+                bv = red_v[w];
+                bi = red_i[w];
+            }
+        slot->v = bv;
+        slot->i = bi;
+        *best = bi;
+    }
+    __syncthreads();
+    return *best;
+}
+
+// Column k's candidate, the candidate's panel row and (owner of k) row k, into column k's slots.
+__device__ __forceinline__ void lu_cta_publish(const double *P, int pitch, int b, int64_t r0,
+                                               int64_t r1, int64_t k, int kc, LuCand *cand,
+                                               double (*crow)[kLuSmemMaxPanel], double *krow,
+                                               double *red_v, long long *red_i, long long *best) {
+    const long long mine =
+        lu_cta_candidate(P, pitch, r0, r1, k, kc, red_v, red_i, &cand[blockIdx.x], best);
+    if (mine != LLONG_MAX)
+        for (int c = threadIdx.x; c < b; c += kLuThreads)
+            __stcg(&crow[blockIdx.x][c], P[(mine - r0) * pitch + c]);
+    if (k >= r0 && k < r1)
+        for (int c = threadIdx.x; c < b; c += kLuThreads)
+            __stcg(&krow[c], P[(k - r0) * pitch + c]);
+}
 
 __global__ void __launch_bounds__(kLuThreads)
     lu_panel_smem_kernel(double *__restrict__ W, int64_t ldw, int64_t n, int64_t ncols, int64_t j,
@@ -312,55 +415,17 @@ __global__ void __launch_bounds__(kLuThreads)
     const int64_t t1 = t0 + per_c < nout ? t0 + per_c : nout;
     __syncthreads();
 
+    // column j's candidate and rows, published before the first barrier
+    lu_cta_publish(P, pitch, b, r0, r1, j, 0, slots->cand[j & 1], slots->crow[j & 1],
+                   slots->krow[j & 1], red_v, red_i, &piv_row);
+    lu_grid_arrive(sync, G, gen);
+
     for (int64_t k = j; k < jb; ++k) {
         const int kc = static_cast<int>(k - j);  // panel column of k
         const int par = static_cast<int>(k & 1);
-        // ---- A: candidate over owned rows >= k; publish it and (owner of k) row k
-        double bv = -1.0;
-        long long bi = LLONG_MAX;
-        for (int64_t i = (r0 > k ? r0 : k) + tid; i < r1; i += kLuThreads) {
-            const double v = fabs(P[(i - r0) * pitch + kc]);
-            if (bi == LLONG_MAX || lu_better(v, i, bv, bi)) {
-                bv = v;
-                bi = i;
-            }
-        }
-#pragma unroll
-        for (int off = 16; off; off >>= 1) {
-            const double ov = __shfl_xor_sync(0xFFFFFFFFu, bv, off);
-            const long long oi = __shfl_xor_sync(0xFFFFFFFFu, bi, off);
-            if (oi != LLONG_MAX && (bi == LLONG_MAX || lu_better(ov, oi, bv, bi))) {
-                bv = ov;
-                bi = oi;
-            }
-        }
-        if (lane == 0) {
-            red_v[warp] = bv;
-            red_i[warp] = bi;
-        }
-        __syncthreads();
-        if (tid == 0) {
-            for (int w = 1; w < kLuThreads / 32; ++w)
-                if (red_i[w] != LLONG_MAX &&
-                    (bi == LLONG_MAX || lu_better(red_v[w], red_i[w], bv, bi))) {
-                    bv = red_v[w];
-                    bi = red_i[w];
-                }
-            slots->cand[par][blockIdx.x].v = bv;
-            slots->cand[par][blockIdx.x].i = bi;
-            piv_row = bi;
-        }
-        __syncthreads();
-        const long long mine = piv_row;
-        if (mine != LLONG_MAX)
-            for (int c = tid; c < b; c += kLuThreads)
-                __stcg(&slots->crow[par][blockIdx.x][c], P[(mine - r0) * pitch + c]);
-        if (k >= r0 && k < r1)
-            for (int c = tid; c < b; c += kLuThreads)
-                __stcg(&slots->krow[par][c], P[(k - r0) * pitch + c]);
-        if (!lu_grid_sync(sync, G, gen, err)) return;
+        if (!lu_grid_wait(sync, gen, err)) return;
 
-        // ---- B: the global pivot, the pivot row, the swap
+        // ---- B: the global pivot, the pivot row, the swap of the panel rows
         lu_global_pivot(slots->cand[par], G, &piv_row, &piv_cta, red_v, red_i, red_b);
         const int64_t p = piv_row;
         const int pcta = piv_cta;
@@ -372,12 +437,6 @@ __global__ void __launch_bounds__(kLuThreads)
             if (p >= r0 && p < r1)  // row p takes old row k
                 for (int c = tid; c < b; c += kLuThreads)
                     P[(p - r0) * pitch + c] = __ldcg(&slots->krow[par][c]);
-            for (int64_t t = t0 + tid; t < t1; t += kLuThreads) {
-                const int64_t c = t < col0 ? t : t + b;
-                const double x = __ldcg(W + k * ldw + c), y = __ldcg(W + p * ldw + c);
-                __stcg(W + k * ldw + c, y);
-                __stcg(W + p * ldw + c, x);
-            }
             if (blockIdx.x == 0 && tid == 0) {
                 const int64_t t = piv[k];
                 piv[k] = piv[p];
@@ -386,26 +445,74 @@ __global__ void __launch_bounds__(kLuThreads)
         }
         __syncthreads();
 
-        // ---- C: scale and update owned rows > k in shared memory: first every row's
-        // multiplier l = W[i, k] / d, one row per thread (the divisions in parallel), then the
-        // rank-1 update of the row's later panel columns, a warp per row
+        // ---- C1: every owned row > k: its multiplier l = W[i, k] / d, then its column k + 1
+        // (one row per thread, the divisions in parallel)
         const double d = urow[kc];
-        if (fabs(d) > 1e-15) {
-            const int64_t i0 = r0 > k + 1 ? r0 : k + 1;
+        const bool upd = fabs(d) > 1e-15;  // the reference skips this column otherwise
+        const int64_t i0 = r0 > k + 1 ? r0 : k + 1;
+        if (upd) {
             for (int64_t i = i0 + tid; i < r1; i += kLuThreads) {
                 double *pi = P + (i - r0) * pitch;
-                pi[kc] = __ddiv_rn(pi[kc], d);
-            }
-            __syncthreads();
-            for (int64_t i = i0 + warp; i < r1; i += kLuThreads / 32) {
-                double *pi = P + (i - r0) * pitch;
-                const double l = pi[kc];
-                for (int c = kc + 1 + lane; c < b; c += 32)
-                    pi[c] = __dsub_rn(pi[c], __dmul_rn(l, urow[c]));
+                const double l = __ddiv_rn(pi[kc], d);
+                pi[kc] = l;
+                if (kc + 1 < b) pi[kc + 1] = __dsub_rn(pi[kc + 1], __dmul_rn(l, urow[kc + 1]));
             }
         }
         __syncthreads();
+
+        // ---- A of column k + 1, ahead of the rest of column k's update: column k + 1 is final
+        // in every row, so the candidate is too; the two rows other CTAs may read (the
+        // candidate and row k + 1) are finished first, published, and the CTA arrives
+        long long done_a = LLONG_MAX, done_b = LLONG_MAX;  // rows already fully updated
+        if (k + 1 < jb) {
+            const int par1 = par ^ 1;
+            const long long mine = lu_cta_candidate(P, pitch, r0, r1, k + 1, kc + 1, red_v, red_i,
+                                                    &slots->cand[par1][blockIdx.x], &piv_row);
+            const bool own1 = k + 1 >= r0 && k + 1 < r1;
+            if (upd) {
+                const int64_t fin = warp == 0 ? mine : (warp == 1 && own1 && k + 1 != mine)
+                                                           ? k + 1 : LLONG_MAX;
+                if (fin != LLONG_MAX) {
+                    double *pi = P + (fin - r0) * pitch;
+                    const double l = pi[kc];
+                    for (int c = kc + 2 + lane; c < b; c += 32)
+                        pi[c] = __dsub_rn(pi[c], __dmul_rn(l, urow[c]));
+                }
+            }
+            __syncthreads();
+            if (mine != LLONG_MAX)
+                for (int c = tid; c < b; c += kLuThreads)
+                    __stcg(&slots->crow[par1][blockIdx.x][c], P[(mine - r0) * pitch + c]);
+            if (own1)
+                for (int c = tid; c < b; c += kLuThreads)
+                    __stcg(&slots->krow[par1][c], P[(k + 1 - r0) * pitch + c]);
+            lu_grid_arrive(sync, G, gen);
+            done_a = mine;
+            done_b = own1 ? k + 1 : LLONG_MAX;
+        }
+
+        // ---- C2: the rest of the rank-1 update (columns k + 2 ..), a warp per row, and the
+        // swap of the columns outside the panel (this CTA's slice), while the others arrive
+        if (upd) {
+            for (int64_t i = i0 + warp; i < r1; i += kLuThreads / 32) {
+                if (i == done_a || i == done_b) continue;
+                double *pi = P + (i - r0) * pitch;
+                const double l = pi[kc];
+                for (int c = kc + 2 + lane; c < b; c += 32)
+                    pi[c] = __dsub_rn(pi[c], __dmul_rn(l, urow[c]));
+            }
+        }
+        if (p != k) {
+            for (int64_t t = t0 + tid; t < t1; t += kLuThreads) {
+                const int64_t c = t < col0 ? t : t + b;
+                const double x = __ldcg(W + k * ldw + c), y = __ldcg(W + p * ldw + c);
+                __stcg(W + k * ldw + c, y);
+                __stcg(W + p * ldw + c, x);
+            }
+        }
+        // the next column's wait ends with a CTA barrier before P or urow is touched again
     }
+    __syncthreads();
 
     for (int e = tid; e < nr * b; e += kLuThreads) {
         const int r = e / b, c = e - r * b;
