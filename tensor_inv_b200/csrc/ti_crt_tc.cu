@@ -317,7 +317,9 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         // ---------------- epilogue (warps 2 .. 2 + kTcEpiWarps) ----------------
         // warp w reads TMEM lane quadrant w % 4 (the unit's columns 32q .. 32q + 31) for the
         // rows r0, r0 + kRowStep, ... of the unit, one output per row and thread.  The
-        // exponents of the next unit are loaded while this one is reconstructed.
+        // exponents of the next unit are loaded while this one is reconstructed, and when C
+        // is updated the next unit's outputs are prefetched into L2, so reading their old
+        // values does not wait on DRAM (no registers held: K3 is at its register cap).
         constexpr int kRowStep = kTcRows / kTcRowsPerThread;
         const int r0 = (warp - 2) >> 2;
         const int q = warp & 3;
@@ -326,16 +328,18 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         GridIter it(P.col_blocks);
         while (it.a < P.row_blocks && tc_skip(P, it.a, it.b)) it.next();
         int ce_n = kNonfiniteExp, re_n[kTcRowsPerThread];
-        auto load_exps = [&](const GridIter &u) {
+        auto load_next = [&](const GridIter &u) {
             const int64_t col = u.b * kTcCols + m;
             ce_n = col < P.cols ? __ldg(P.col_exp + col) : kNonfiniteExp;
 #pragma unroll
             for (int k = 0; k < kTcRowsPerThread; ++k) {
                 const int64_t row = u.a * kTcRows + r0 + k * kRowStep;
                 re_n[k] = row < P.rows ? __ldg(P.row_exp + row) : kNonfiniteExp;
+                if (kOutMode != 0 && row < P.rows && col < P.cols)
+                    asm volatile("prefetch.global.L2 [%0];" ::"l"(P.C + row * P.ldc + col));
             }
         };
-        if (it.a < P.row_blocks) load_exps(it);
+        if (it.a < P.row_blocks) load_next(it);
         int64_t local = 0;
         while (it.a < P.row_blocks) {
             const int64_t ua = it.a, ub = it.b;
@@ -346,7 +350,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
             do {
                 it.next();
             } while (it.a < P.row_blocks && tc_skip(P, it.a, it.b));
-            if (it.a < P.row_blocks) load_exps(it);
+            if (it.a < P.row_blocks) load_next(it);
             const int acc = static_cast<int>(local % kTcAcc);
             const uint32_t acc_phase = static_cast<uint32_t>((local / kTcAcc) & 1);
             ++local;
