@@ -3,6 +3,11 @@
 Same algorithm and arithmetic as the reference (src/tensor_inv/cholesky.py:6-35).  The
 trailing update ``W[jb:, jb:] -= crt_matmul(L21, L21.T)`` runs fused on CUDA
 (``crt_matmul_update``) with ``L21.T`` consumed as a transposed view (no copy).
+
+On CUDA the diagonal blocks go through ``torch.linalg.cholesky_ex``, the same factorization
+as the reference's ``torch.linalg.cholesky`` without its per-call host synchronisation for
+the error check; the blocks' error codes are checked once at the end, and the first failing
+block raises the error ``torch.linalg.cholesky`` would have raised there.
 """
 
 import torch
@@ -22,13 +27,18 @@ def cholesky(A, block_size=64):
     n = A.shape[0]
     L = torch.zeros_like(A)
     W = A.clone()
+    infos = [] if A.is_cuda else None  # error codes of the diagonal blocks, checked at the end
 
     for j in range(0, n, block_size):
         b = min(block_size, n - j)
         jb = j + b
 
         # panel: small Cholesky on the diagonal block (cholesky.py:24)
-        L[j:jb, j:jb] = torch.linalg.cholesky(W[j:jb, j:jb])
+        if infos is None:
+            L[j:jb, j:jb] = torch.linalg.cholesky(W[j:jb, j:jb])
+        else:
+            L[j:jb, j:jb], info = torch.linalg.cholesky_ex(W[j:jb, j:jb])
+            infos.append(info)
 
         if jb < n:
             # panel: triangular solve for the sub-diagonal block (cholesky.py:28-30)
@@ -46,4 +56,17 @@ def cholesky(A, block_size=64):
             else:
                 W[jb:, jb:] -= crt_matmul(L21, L21.T, moduli=mods)
 
+    if infos:
+        _raise_first_failure(torch.stack(infos).cpu())
     return L
+
+
+def _raise_first_failure(infos):
+    """torch.linalg.cholesky's error for the first diagonal block whose factorization failed
+    (info = the order of its first leading minor that is not positive-definite)."""
+    bad = torch.nonzero(infos)
+    if bad.numel():
+        order = int(infos[bad[0, 0]])
+        raise torch.linalg.LinAlgError(
+            "linalg.cholesky: The factorization could not be completed because the input is not "
+            f"positive-definite (the leading minor of order {order} is not positive-definite).")

@@ -48,3 +48,44 @@ def test_cholesky_lower_update_is_bit_identical(monkeypatch):
     monkeypatch.setattr(ch, "crt_matmul_update", update_full)
     L_full = cholesky(A, block_size=128)
     assert torch.equal(L_low.view(torch.int64), L_full.view(torch.int64))
+
+
+def _reference_loop(A, block_size):
+    """The reference's blocked loop (cholesky.py:6-35) with torch.linalg.cholesky per block."""
+    from tensor_inv_b200.crt_matmul import crt_matmul
+
+    n = A.shape[0]
+    L = torch.zeros_like(A)
+    W = A.clone()
+    for j in range(0, n, block_size):
+        jb = min(j + block_size, n)
+        L[j:jb, j:jb] = torch.linalg.cholesky(W[j:jb, j:jb])
+        if jb < n:
+            L[jb:, j:jb] = torch.linalg.solve_triangular(
+                L[j:jb, j:jb], W[jb:, j:jb].T, upper=False).T
+            L21 = L[jb:, j:jb]
+            W[jb:, jb:] -= crt_matmul(L21, L21.T)
+    return L
+
+
+def test_cholesky_matches_reference_loop_bitwise():
+    """The diagonal blocks through cholesky_ex (no host sync per block) give the reference
+    loop's L bit for bit."""
+    g = torch.Generator().manual_seed(7)
+    X = torch.randn(700, 700, generator=g, dtype=torch.float64)
+    A = (X @ X.T / 700 + 1e-3 * torch.eye(700, dtype=torch.float64)).cuda()
+    got = cholesky(A, block_size=256)
+    want = _reference_loop(A, 256)
+    assert torch.equal(got.view(torch.int64), want.view(torch.int64))
+
+
+def test_cholesky_not_positive_definite_raises_torch_error():
+    """A block that fails raises what torch.linalg.cholesky raises on that block."""
+    A = torch.eye(600, dtype=torch.float64)
+    A[300, 300] = -1.0  # the second diagonal block (rows 256..511) fails at its minor 45
+    with pytest.raises(torch.linalg.LinAlgError) as want:
+        torch.linalg.cholesky(A[256:512, 256:512])
+    with pytest.raises(torch.linalg.LinAlgError) as got:
+        cholesky(A.cuda(), block_size=256)
+    assert str(got.value) == str(want.value)
+    assert "order 45 " in str(got.value)
