@@ -13,11 +13,12 @@
 //
 // One launch per panel replaces the reference's 8 small launches and 2 host round trips per
 // column.  CTAs (launched cooperatively, so all are resident at once) own contiguous row
-// ranges of the panel.  Each column takes two grid barriers: after the per-CTA argmax
-// candidates (every CTA then reduces the same candidates in the same order, so all agree on
-// p), and after the row swap (the update reads the pivot row).  The barrier is a counter and
-// a generation word in the caller's workspace; every wait is bounded in time, and on timeout
-// the kernel records an error and all CTAs return.  All accesses to W bypass L1 (ld/st .cg), so
+// ranges of the panel.  In the global-memory variant each column takes two grid barriers:
+// after the per-CTA argmax candidates (every CTA then reduces the same candidates in the same
+// total order, so all agree on p), and after the row swap (the update reads the pivot row).
+// The shared-memory variant below needs one per column.  The barriers' words live in the
+// caller's workspace; every wait is bounded in time, and on timeout the kernel records an
+// error and all CTAs return.  All accesses to W bypass L1 (ld/st .cg), so
 // a CTA never reads a stale copy of a row that another CTA swapped or updated.
 #include <cstring>
 
@@ -107,26 +108,32 @@ __device__ bool lu_grid_sync(LuSync *s, unsigned nblocks, unsigned &gen_local, i
     return ok_sh != 0;
 }
 
-// lu_grid_sync in two halves, so a CTA can work between its arrival and its wait.
-// lu_grid_arrive: called by every thread after the CTA's writes that the other CTAs read.
-__device__ __forceinline__ void lu_grid_arrive(LuSync *s, unsigned nblocks, unsigned &gen_local) {
-    __syncthreads();
-    const unsigned target = gen_local + 1;
-    if (threadIdx.x == 0 && lu_atom_add_acq_rel(&s->count, 1u) == nblocks - 1) {
-        s->count = 0u;  // ordered before the release below
-        lu_st_release(&s->gen, target);
-    }
-    gen_local = target;
+// A split grid barrier on a count of arrivals that only grows during a launch (the host zeroes
+// it first): barrier t is complete once the count reaches t * G.  Thread 0 arrives with a
+// release reduction (no value returned, so it does not wait for the L2 round trip) after a CTA
+// barrier, so the arrival carries the CTA's writes; waiters poll the count with acquire loads.
+// A CTA can only arrive at barrier t + 1 after its own wait for t, so the count is below
+// (t + 2) * G while any CTA waits for t.
+__device__ __forceinline__ void lu_red_release_add(unsigned *p, unsigned v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// lu_grid_wait: until every CTA has arrived at generation gen_local (bounded; false in every
-// thread if the wait ran out or another CTA gave up).  Ends with a CTA barrier.
-__device__ bool lu_grid_wait(LuSync *s, unsigned gen_local, int *err) {
+// lu_grid_arrive: called by every thread after the CTA's writes that the other CTAs read;
+// advances `target` to the count that completes this barrier.
+__device__ __forceinline__ void lu_grid_arrive(LuSync *s, unsigned nblocks, unsigned &target) {
+    __syncthreads();
+    if (threadIdx.x == 0) lu_red_release_add(&s->count, 1u);
+    target += nblocks;
+}
+
+// lu_grid_wait: until the count of arrivals reaches `target` (bounded; false in every thread if
+// the wait ran out or another CTA gave up).  Ends with a CTA barrier.
+__device__ bool lu_grid_wait(LuSync *s, unsigned target, int *err) {
     __shared__ int ok_sh;
     if (threadIdx.x == 0) {
         int ok = 1;
         const unsigned long long t0 = globaltimer_ns();
-        while (lu_ld_acquire(&s->gen) != gen_local) {
+        while (static_cast<int>(lu_ld_acquire(&s->count) - target) < 0) {
             if (*reinterpret_cast<volatile int *>(&s->abort)) {
                 ok = 0;
                 break;
@@ -144,12 +151,42 @@ __device__ bool lu_grid_wait(LuSync *s, unsigned gen_local, int *err) {
     return ok_sh != 0;
 }
 
+// The best of the eight warps' candidates in red_*, computed by every warp: lanes 0..7 take one
+// warp's candidate each and an xor-shuffle tree over them leaves the best in lane 0, which is
+// broadcast.  The order (NaN first, then value, then the smaller index) is strict and total on
+// distinct rows, so every warp, and every CTA reducing the same values, picks the same one as
+// any other reduction order would.  red_b may be null (no CTA indices).
+__device__ __forceinline__ void lu_reduce_warps(const double *red_v, const long long *red_i,
+                                                const int *red_b, double &bv, long long &bi,
+                                                int &bb) {
+    constexpr int kW = kLuThreads / 32;
+    const int lane = threadIdx.x & 31;
+    bv = lane < kW ? red_v[lane] : -1.0;
+    bi = lane < kW ? red_i[lane] : LLONG_MAX;
+    bb = lane < kW && red_b ? red_b[lane] : 0;
+#pragma unroll
+    for (int off = kW / 2; off; off >>= 1) {
+        const double ov = __shfl_xor_sync(0xFFFFFFFFu, bv, off);
+        const long long oi = __shfl_xor_sync(0xFFFFFFFFu, bi, off);
+        const int ob = __shfl_xor_sync(0xFFFFFFFFu, bb, off);
+        if (oi != LLONG_MAX && (bi == LLONG_MAX || lu_better(ov, oi, bv, bi))) {
+            bv = ov;
+            bi = oi;
+            bb = ob;
+        }
+    }
+    bv = __shfl_sync(0xFFFFFFFFu, bv, 0);
+    bi = __shfl_sync(0xFFFFFFFFu, bi, 0);
+    bb = __shfl_sync(0xFFFFFFFFu, bb, 0);
+}
+
 // The global pivot from the G published candidates: thread t loads candidate t (all loads in
-// flight at once), then a warp and a block reduction.  Every CTA reduces the same values with
-// the same total order (value, then index), so all CTAs agree.  Returns the row in *row and the
-// publishing CTA in *cta (block-uniform, through shared memory).
-__device__ __forceinline__ void lu_global_pivot(const LuCand *cands, unsigned G, long long *row,
-                                                int *cta, double *red_v, long long *red_i,
+// flight at once), then a warp reduction and, in every warp, the reduction of the eight warps'
+// results (lu_reduce_warps).  Every CTA reduces the same values in the same total order, so all
+// agree.  Returns the row and the publishing CTA in every thread.  red_* are read after the CTA
+// barrier inside; the caller passes another CTA barrier before they are written again.
+__device__ __forceinline__ void lu_global_pivot(const LuCand *cands, unsigned G, long long &row,
+                                                int &cta, double *red_v, long long *red_i,
                                                 int *red_b) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     double bv = -1.0;
@@ -181,17 +218,9 @@ __device__ __forceinline__ void lu_global_pivot(const LuCand *cands, unsigned G,
         red_b[warp] = bb;
     }
     __syncthreads();
-    if (tid == 0) {
-        for (int w = 1; w < kLuThreads / 32; ++w)
-            if (red_i[w] != LLONG_MAX && (bi == LLONG_MAX || lu_better(red_v[w], red_i[w], bv, bi))) {
-                bv = red_v[w];
-                bi = red_i[w];
-                bb = red_b[w];
-            }
-        *row = bi;
-        *cta = bb;
-    }
-    __syncthreads();
+    lu_reduce_warps(red_v, red_i, red_b, bv, bi, bb);
+    row = bi;
+    cta = bb;
 }
 
 __global__ void __launch_bounds__(kLuThreads)
@@ -202,8 +231,6 @@ __global__ void __launch_bounds__(kLuThreads)
     __shared__ double red_v[kLuThreads / 32];
     __shared__ long long red_i[kLuThreads / 32];
     __shared__ int red_b[kLuThreads / 32];
-    __shared__ long long piv_row;
-    __shared__ int piv_cta;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const unsigned G = gridDim.x;
     const int64_t rows = n - j;
@@ -250,8 +277,10 @@ __global__ void __launch_bounds__(kLuThreads)
         if (!lu_grid_sync(sync, G, gen, err)) return;
 
         // ---- B: the global pivot, then the row swap
-        lu_global_pivot(cand, G, &piv_row, &piv_cta, red_v, red_i, red_b);
-        const int64_t p = piv_row;
+        long long p_row;
+        int p_cta;
+        lu_global_pivot(cand, G, p_row, p_cta, red_v, red_i, red_b);
+        const int64_t p = p_row;
         if (p != k) {
             const int64_t per_c = (ncols + G - 1) / G;
             const int64_t c0 = int64_t(blockIdx.x) * per_c;
@@ -324,12 +353,13 @@ struct LuSlots {
     double crow[2][kLuSmemMaxCtas][kLuSmemMaxPanel];
 };
 
-// This CTA's argmax candidate for column k (panel column kc of P) over its rows >= k.  Thread 0
-// writes it to *slot and to *best (shared); every thread returns it.
+// This CTA's argmax candidate for column k (panel column kc of P) over its rows >= k, returned
+// in every thread; thread 0 writes it to *slot.  red_* are read after the CTA barrier inside;
+// the caller passes another CTA barrier before they are written again.
 __device__ __forceinline__ long long lu_cta_candidate(const double *P, int pitch, int64_t r0,
                                                       int64_t r1, int64_t k, int kc,
                                                       double *red_v, long long *red_i,
-                                                      LuCand *slot, long long *best) {
+                                                      LuCand *slot) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     double bv = -1.0;
     long long bi = LLONG_MAX;
@@ -354,28 +384,22 @@ __device__ __forceinline__ long long lu_cta_candidate(const double *P, int pitch
         red_i[warp] = bi;
     }
     __syncthreads();
+    int unused;
+    lu_reduce_warps(red_v, red_i, nullptr, bv, bi, unused);
     if (tid == 0) {
-        for (int w = 1; w < kLuThreads / 32; ++w)
-            if (red_i[w] != LLONG_MAX &&
-                (bi == LLONG_MAX || lu_better(red_v[w], red_i[w], bv, bi))) {
-                bv = red_v[w];
-                bi = red_i[w];
-            }
         slot->v = bv;
         slot->i = bi;
-        *best = bi;
     }
-    __syncthreads();
-    return *best;
+    return bi;
 }
 
 // Column k's candidate, the candidate's panel row and (owner of k) row k, into column k's slots.
 __device__ __forceinline__ void lu_cta_publish(const double *P, int pitch, int b, int64_t r0,
                                                int64_t r1, int64_t k, int kc, LuCand *cand,
                                                double (*crow)[kLuSmemMaxPanel], double *krow,
-                                               double *red_v, long long *red_i, long long *best) {
+                                               double *red_v, long long *red_i) {
     const long long mine =
-        lu_cta_candidate(P, pitch, r0, r1, k, kc, red_v, red_i, &cand[blockIdx.x], best);
+        lu_cta_candidate(P, pitch, r0, r1, k, kc, red_v, red_i, &cand[blockIdx.x]);
     if (mine != LLONG_MAX)
         for (int c = threadIdx.x; c < b; c += kLuThreads)
             __stcg(&crow[blockIdx.x][c], P[(mine - r0) * pitch + c]);
@@ -393,8 +417,6 @@ __global__ void __launch_bounds__(kLuThreads)
     __shared__ double red_v[kLuThreads / 32];
     __shared__ long long red_i[kLuThreads / 32];
     __shared__ int red_b[kLuThreads / 32];
-    __shared__ long long piv_row;
-    __shared__ int piv_cta;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const unsigned G = gridDim.x;
     const int b = static_cast<int>(jb - j), pitch = b + 1;
@@ -402,7 +424,7 @@ __global__ void __launch_bounds__(kLuThreads)
     const int64_t r0 = j + int64_t(blockIdx.x) * per;
     const int64_t r1 = r0 + per < n ? r0 + per : n;
     const int nr = r1 > r0 ? static_cast<int>(r1 - r0) : 0;
-    unsigned gen = 0;
+    unsigned arrivals = 0;  // the count of arrivals that completes the next barrier
 
     for (int e = tid; e < nr * b; e += kLuThreads) {
         const int r = e / b, c = e - r * b;
@@ -417,18 +439,19 @@ __global__ void __launch_bounds__(kLuThreads)
 
     // column j's candidate and rows, published before the first barrier
     lu_cta_publish(P, pitch, b, r0, r1, j, 0, slots->cand[j & 1], slots->crow[j & 1],
-                   slots->krow[j & 1], red_v, red_i, &piv_row);
-    lu_grid_arrive(sync, G, gen);
+                   slots->krow[j & 1], red_v, red_i);
+    lu_grid_arrive(sync, G, arrivals);
 
     for (int64_t k = j; k < jb; ++k) {
         const int kc = static_cast<int>(k - j);  // panel column of k
         const int par = static_cast<int>(k & 1);
-        if (!lu_grid_wait(sync, gen, err)) return;
+        if (!lu_grid_wait(sync, arrivals, err)) return;
 
         // ---- B: the global pivot, the pivot row, the swap of the panel rows
-        lu_global_pivot(slots->cand[par], G, &piv_row, &piv_cta, red_v, red_i, red_b);
-        const int64_t p = piv_row;
-        const int pcta = piv_cta;
+        long long p_row;
+        int pcta;
+        lu_global_pivot(slots->cand[par], G, p_row, pcta, red_v, red_i, red_b);
+        const int64_t p = p_row;
         for (int c = tid; c < b; c += kLuThreads) urow[c] = __ldcg(&slots->crow[par][pcta][c]);
         if (p != k) {
             if (k >= r0 && k < r1)  // row k takes old row p
@@ -467,7 +490,7 @@ __global__ void __launch_bounds__(kLuThreads)
         if (k + 1 < jb) {
             const int par1 = par ^ 1;
             const long long mine = lu_cta_candidate(P, pitch, r0, r1, k + 1, kc + 1, red_v, red_i,
-                                                    &slots->cand[par1][blockIdx.x], &piv_row);
+                                                    &slots->cand[par1][blockIdx.x]);
             const bool own1 = k + 1 >= r0 && k + 1 < r1;
             if (upd) {
                 const int64_t fin = warp == 0 ? mine : (warp == 1 && own1 && k + 1 != mine)
@@ -486,7 +509,7 @@ __global__ void __launch_bounds__(kLuThreads)
             if (own1)
                 for (int c = tid; c < b; c += kLuThreads)
                     __stcg(&slots->krow[par1][c], P[(k + 1 - r0) * pitch + c]);
-            lu_grid_arrive(sync, G, gen);
+            lu_grid_arrive(sync, G, arrivals);
             done_a = mine;
             done_b = own1 ? k + 1 : LLONG_MAX;
         }
