@@ -71,6 +71,27 @@ def test_device_panel_is_bit_identical(monkeypatch, n, block, make):
         assert err < 1e-10
 
 
+def _same_bits_or_nan(a, b):
+    a, b = a.contiguous(), b.contiguous()
+    na, nb = torch.isnan(a), torch.isnan(b)
+    if not torch.equal(na, nb):
+        return False
+    return torch.equal(a.masked_fill(na, 0).view(torch.int64), b.masked_fill(nb, 0).view(torch.int64))
+
+
+def test_device_panel_nan_pivots(monkeypatch):
+    """NaN counts as the largest |entry| (torch.argmax), the first NaN row wins, and a NaN
+    pivot fails the 1e-15 test, so the column is skipped: the device panel does the same."""
+    g = torch.Generator().manual_seed(12)
+    A = torch.randn(300, 300, generator=g, dtype=torch.float64)
+    A[150, 3] = float("nan")
+    A[90, 3] = float("nan")    # two NaNs in one column: the smaller row index is the pivot
+    A[200, 70] = float("nan")  # and one in a later panel
+    (P0, L0, U0), (P1, L1, U1) = _lu_both(A.cuda(), 64, monkeypatch)
+    assert torch.equal(P0, P1)
+    assert _same_bits_or_nan(L0, L1) and _same_bits_or_nan(U0, U1)
+
+
 def test_device_panel_transposed_input(monkeypatch):
     g = torch.Generator().manual_seed(11)
     A = torch.randn(150, 150, generator=g, dtype=torch.float64).cuda().t()  # column-major view
