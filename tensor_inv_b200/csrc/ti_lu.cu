@@ -330,36 +330,48 @@ __global__ void __launch_bounds__(kLuThreads)
 // ---------------------------------------------------------------------------------------
 // Shared-memory variant: each CTA keeps its panel rows (all b columns) in shared memory for
 // the whole panel, so the column updates never touch global memory, and one grid barrier per
-// column suffices.  Before column k's barrier every CTA publishes its argmax candidate and
-// that candidate's panel row, and the owner of row k publishes row k (double-buffered by
-// column parity: a CTA can only write column k+1's slots after every CTA has passed column k's
-// barrier, and it reads column k's slots before arriving at column k+1's).  After the barrier
-// every CTA takes the pivot row from the winner's slot; the owners of rows k and p swap their
-// panel parts from the slots.
+// column suffices.  Before column k's barrier every CTA publishes its argmax candidate (with
+// the candidate row's values at columns k and k+1) and that candidate's panel row, and the
+// owner of row k publishes row k and, apart, its values at columns k and k+1 (all
+// double-buffered by column parity: a CTA can only write column k+1's slots after every CTA
+// has passed column k's barrier, and it reads column k's slots before arriving at column
+// k+1's).  After the barrier every CTA reduces the candidates to the pivot row p; those loads
+// also bring the pivot W[p, k], W[p, k+1] and old row k's W[k, k], W[k, k+1], which are all
+// that the multipliers and the update of column k+1 need, so those run while the full pivot
+// row (and, for the owner of p, old row k) are still on their way from L2 into registers.
 // The barrier is split into an arrival and a wait, and column k+1's candidate is found ahead
 // of the rest of column k's update: each CTA divides its rows' multipliers and updates
-// column k+1 only, takes its candidate for column k+1, finishes the two rows it may publish
-// (the candidate and row k+1), publishes and arrives; the rest of the rank-1 update
-// (columns k+2 ..) and the swap of the columns outside the panel (in global memory, each
-// CTA always on the same column slice, so its swaps stay in program order) run while the
-// other CTAs arrive.  Every element receives the same operations in the same order.
+// column k+1 only, takes its candidate for column k+1, places the swapped rows, finishes the
+// two rows it may publish (the candidate and row k+1), publishes and arrives; the rest of the
+// rank-1 update (columns k+2 ..) and the swap of the columns outside the panel (in global
+// memory, each CTA always on the same column slice, so its swaps stay in program order) run
+// while the other CTAs arrive.  Every element receives the same operations in the same order.
 // ---------------------------------------------------------------------------------------
 constexpr int kLuSmemMaxPanel = 256;
 constexpr int kLuSmemMaxCtas = 256;
+static_assert(kLuSmemMaxPanel <= kLuThreads && kLuSmemMaxCtas <= kLuThreads,
+              "one thread per panel column and per candidate");
+
+struct LuCandRow {
+    double d;      // the candidate row's W[i, k]; |d| ranks the candidates
+    long long i;   // the row, LLONG_MAX if the CTA has no rows >= k
+    double u1;     // the candidate row's W[i, k + 1] (0 past the panel)
+    double pad;
+};
 
 struct LuSlots {
-    LuCand cand[2][kLuSmemMaxCtas];
+    LuCandRow cand[2][kLuSmemMaxCtas];
+    double khead[2][2];  // W[k, k], W[k, k + 1] of row k before the swap
     double krow[2][kLuSmemMaxPanel];
     double crow[2][kLuSmemMaxCtas][kLuSmemMaxPanel];
 };
 
 // This CTA's argmax candidate for column k (panel column kc of P) over its rows >= k, returned
-// in every thread; thread 0 writes it to *slot.  red_* are read after the CTA barrier inside;
-// the caller passes another CTA barrier before they are written again.
+// in every thread.  red_* are read after the CTA barrier inside; the caller passes another CTA
+// barrier before they are written again.
 __device__ __forceinline__ long long lu_cta_candidate(const double *P, int pitch, int64_t r0,
                                                       int64_t r1, int64_t k, int kc,
-                                                      double *red_v, long long *red_i,
-                                                      LuCand *slot) {
+                                                      double *red_v, long long *red_i) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     double bv = -1.0;
     long long bi = LLONG_MAX;
@@ -386,29 +398,95 @@ __device__ __forceinline__ long long lu_cta_candidate(const double *P, int pitch
     __syncthreads();
     int unused;
     lu_reduce_warps(red_v, red_i, nullptr, bv, bi, unused);
-    if (tid == 0) {
-        slot->v = bv;
-        slot->i = bi;
-    }
     return bi;
 }
 
-// Column k's candidate, the candidate's panel row and (owner of k) row k, into column k's slots.
-__device__ __forceinline__ void lu_cta_publish(const double *P, int pitch, int b, int64_t r0,
-                                               int64_t r1, int64_t k, int kc, LuCand *cand,
-                                               double (*crow)[kLuSmemMaxPanel], double *krow,
-                                               double *red_v, long long *red_i) {
-    const long long mine =
-        lu_cta_candidate(P, pitch, r0, r1, k, kc, red_v, red_i, &cand[blockIdx.x]);
+// Column k's slots (panel column kc): the candidate `mine` with its values at kc and kc+1,
+// its panel row, and (owner of row k) row k with, apart, its values at kc and kc+1.
+__device__ __forceinline__ void lu_publish(LuSlots *slots, int par, const double *P, int pitch,
+                                           int b, int64_t r0, int64_t r1, int64_t k, int kc,
+                                           long long mine) {
+    const int tid = threadIdx.x;
+    const bool own_k = k >= r0 && k < r1;
     if (mine != LLONG_MAX)
-        for (int c = threadIdx.x; c < b; c += kLuThreads)
-            __stcg(&crow[blockIdx.x][c], P[(mine - r0) * pitch + c]);
-    if (k >= r0 && k < r1)
-        for (int c = threadIdx.x; c < b; c += kLuThreads)
-            __stcg(&krow[c], P[(k - r0) * pitch + c]);
+        for (int c = tid; c < b; c += kLuThreads)
+            __stcg(&slots->crow[par][blockIdx.x][c], P[(mine - r0) * pitch + c]);
+    if (own_k)
+        for (int c = tid; c < b; c += kLuThreads)
+            __stcg(&slots->krow[par][c], P[(k - r0) * pitch + c]);
+    if (tid == 0) {
+        LuCandRow *s = &slots->cand[par][blockIdx.x];
+        const double *pm = mine != LLONG_MAX ? P + (mine - r0) * pitch : nullptr;
+        __stcg(&s->d, pm ? pm[kc] : 0.0);
+        __stcg(&s->i, mine);
+        __stcg(&s->u1, pm && kc + 1 < b ? pm[kc + 1] : 0.0);
+    }
+    if (tid == 32 && own_k) {
+        const double *pk = P + (k - r0) * pitch;
+        __stcg(&slots->khead[par][0], pk[kc]);
+        __stcg(&slots->khead[par][1], kc + 1 < b ? pk[kc + 1] : 0.0);
+    }
 }
 
-__global__ void __launch_bounds__(kLuThreads)
+// The pivot from column k's G published candidates (thread t loads candidate t), with the
+// pivot row's values at columns k and k+1 and old row k's (from the header slot), in every
+// thread.  `bc` is 4 doubles of shared memory.  Every CTA reduces the same values in the same
+// total order, so all agree.  red_* and bc are read after the CTA barriers inside; the caller
+// passes another CTA barrier before they are written again.
+__device__ __forceinline__ void lu_smem_pivot(const LuCandRow *cands, const double *khead,
+                                              unsigned G, long long &row, int &cta, double &d,
+                                              double &u1, double &k0, double &k1, double *red_v,
+                                              long long *red_i, int *red_b, double *bc) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    double bv = -1.0, dv = 0.0, uv = 0.0;
+    long long bi = LLONG_MAX;
+    int bb = 0;
+    if (tid < static_cast<int>(G)) {
+        const long long i = __ldcg(&cands[tid].i);
+        dv = __ldcg(&cands[tid].d);
+        uv = __ldcg(&cands[tid].u1);
+        if (i != LLONG_MAX) {
+            bv = fabs(dv);
+            bi = i;
+            bb = tid;
+        }
+    }
+    if (tid == kLuThreads - 1) {
+        bc[2] = __ldcg(&khead[0]);
+        bc[3] = __ldcg(&khead[1]);
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) {
+        const double ov = __shfl_xor_sync(0xFFFFFFFFu, bv, off);
+        const long long oi = __shfl_xor_sync(0xFFFFFFFFu, bi, off);
+        const int ob = __shfl_xor_sync(0xFFFFFFFFu, bb, off);
+        if (oi != LLONG_MAX && (bi == LLONG_MAX || lu_better(ov, oi, bv, bi))) {
+            bv = ov;
+            bi = oi;
+            bb = ob;
+        }
+    }
+    if (lane == 0) {
+        red_v[warp] = bv;
+        red_i[warp] = bi;
+        red_b[warp] = bb;
+    }
+    __syncthreads();
+    lu_reduce_warps(red_v, red_i, red_b, bv, bi, bb);
+    if (tid == bb) {  // the thread that loaded the winner holds its values
+        bc[0] = dv;
+        bc[1] = uv;
+    }
+    __syncthreads();
+    row = bi;
+    cta = bb;
+    d = bc[0];
+    u1 = bc[1];
+    k0 = bc[2];
+    k1 = bc[3];
+}
+
+__global__ void __launch_bounds__(kLuThreads, 1)
     lu_panel_smem_kernel(double *__restrict__ W, int64_t ldw, int64_t n, int64_t ncols, int64_t j,
                          int64_t jb, int64_t col0, int64_t *__restrict__ piv, LuSync *sync,
                          LuSlots *slots, int *err) {
@@ -417,6 +495,7 @@ __global__ void __launch_bounds__(kLuThreads)
     __shared__ double red_v[kLuThreads / 32];
     __shared__ long long red_i[kLuThreads / 32];
     __shared__ int red_b[kLuThreads / 32];
+    __shared__ double bc[4];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const unsigned G = gridDim.x;
     const int b = static_cast<int>(jb - j), pitch = b + 1;
@@ -437,9 +516,11 @@ __global__ void __launch_bounds__(kLuThreads)
     const int64_t t1 = t0 + per_c < nout ? t0 + per_c : nout;
     __syncthreads();
 
-    // column j's candidate and rows, published before the first barrier
-    lu_cta_publish(P, pitch, b, r0, r1, j, 0, slots->cand[j & 1], slots->crow[j & 1],
-                   slots->krow[j & 1], red_v, red_i);
+    // column j's slots, published before the first barrier
+    {
+        const long long mine = lu_cta_candidate(P, pitch, r0, r1, j, 0, red_v, red_i);
+        lu_publish(slots, static_cast<int>(j & 1), P, pitch, b, r0, r1, j, 0, mine);
+    }
     lu_grid_arrive(sync, G, arrivals);
 
     for (int64_t k = j; k < jb; ++k) {
@@ -447,50 +528,67 @@ __global__ void __launch_bounds__(kLuThreads)
         const int par = static_cast<int>(k & 1);
         if (!lu_grid_wait(sync, arrivals, err)) return;
 
-        // ---- B: the global pivot, the pivot row, the swap of the panel rows
+        // ---- B: the pivot and the values the multipliers need; the full pivot row and (owner
+        // of p) old row k start towards registers
         long long p_row;
         int pcta;
-        lu_global_pivot(slots->cand[par], G, p_row, pcta, red_v, red_i, red_b);
+        double d, u1, k0, k1;
+        lu_smem_pivot(slots->cand[par], slots->khead[par], G, p_row, pcta, d, u1, k0, k1, red_v,
+                      red_i, red_b, bc);
         const int64_t p = p_row;
-        for (int c = tid; c < b; c += kLuThreads) urow[c] = __ldcg(&slots->crow[par][pcta][c]);
-        if (p != k) {
-            if (k >= r0 && k < r1)  // row k takes old row p
-                for (int c = tid; c < b; c += kLuThreads)
-                    P[(k - r0) * pitch + c] = __ldcg(&slots->crow[par][pcta][c]);
-            if (p >= r0 && p < r1)  // row p takes old row k
-                for (int c = tid; c < b; c += kLuThreads)
-                    P[(p - r0) * pitch + c] = __ldcg(&slots->krow[par][c]);
-            if (blockIdx.x == 0 && tid == 0) {
-                const int64_t t = piv[k];
-                piv[k] = piv[p];
-                piv[p] = t;
-            }
+        const bool own_k = k >= r0 && k < r1;
+        const bool own_p = p != k && p >= r0 && p < r1;
+        double ru = 0.0, rk = 0.0;
+        if (tid < b) {
+            ru = __ldcg(&slots->crow[par][pcta][tid]);
+            if (own_p) rk = __ldcg(&slots->krow[par][tid]);
         }
-        __syncthreads();
 
         // ---- C1: every owned row > k: its multiplier l = W[i, k] / d, then its column k + 1
-        // (one row per thread, the divisions in parallel)
-        const double d = urow[kc];
+        // (one row per thread, the divisions in parallel).  Row p already holds old row k
+        // here: its two values come from the header slot.
         const bool upd = fabs(d) > 1e-15;  // the reference skips this column otherwise
         const int64_t i0 = r0 > k + 1 ? r0 : k + 1;
         if (upd) {
             for (int64_t i = i0 + tid; i < r1; i += kLuThreads) {
                 double *pi = P + (i - r0) * pitch;
-                const double l = __ddiv_rn(pi[kc], d);
+                const bool sw = i == p;
+                const double l = __ddiv_rn(sw ? k0 : pi[kc], d);
                 pi[kc] = l;
-                if (kc + 1 < b) pi[kc + 1] = __dsub_rn(pi[kc + 1], __dmul_rn(l, urow[kc + 1]));
+                if (kc + 1 < b)
+                    pi[kc + 1] = __dsub_rn(sw ? k1 : pi[kc + 1], __dmul_rn(l, u1));
             }
+        } else if (own_p && tid == 0) {
+            double *pp = P + (p - r0) * pitch;
+            pp[kc] = k0;
+            if (kc + 1 < b) pp[kc + 1] = k1;
         }
         __syncthreads();
 
         // ---- A of column k + 1, ahead of the rest of column k's update: column k + 1 is final
-        // in every row, so the candidate is too; the two rows other CTAs may read (the
-        // candidate and row k + 1) are finished first, published, and the CTA arrives
+        // in every row, so the candidate is too
+        const long long mine =
+            k + 1 < jb ? lu_cta_candidate(P, pitch, r0, r1, k + 1, kc + 1, red_v, red_i)
+                       : LLONG_MAX;
+
+        // ---- the swap: row k takes the pivot row, row p old row k (its columns k and k + 1
+        // were written above)
+        if (tid < b) {
+            urow[tid] = ru;
+            if (own_k && p != k) P[(k - r0) * pitch + tid] = ru;
+            if (own_p && tid != kc && tid != kc + 1) P[(p - r0) * pitch + tid] = rk;
+        }
+        if (p != k && blockIdx.x == 0 && tid == 0) {
+            const int64_t t = piv[k];
+            piv[k] = piv[p];
+            piv[p] = t;
+        }
+        __syncthreads();
+
+        // ---- the two rows other CTAs may read (the candidate and row k + 1) are finished
+        // first, published, and the CTA arrives
         long long done_a = LLONG_MAX, done_b = LLONG_MAX;  // rows already fully updated
         if (k + 1 < jb) {
-            const int par1 = par ^ 1;
-            const long long mine = lu_cta_candidate(P, pitch, r0, r1, k + 1, kc + 1, red_v, red_i,
-                                                    &slots->cand[par1][blockIdx.x]);
             const bool own1 = k + 1 >= r0 && k + 1 < r1;
             if (upd) {
                 const int64_t fin = warp == 0 ? mine : (warp == 1 && own1 && k + 1 != mine)
@@ -503,12 +601,7 @@ __global__ void __launch_bounds__(kLuThreads)
                 }
             }
             __syncthreads();
-            if (mine != LLONG_MAX)
-                for (int c = tid; c < b; c += kLuThreads)
-                    __stcg(&slots->crow[par1][blockIdx.x][c], P[(mine - r0) * pitch + c]);
-            if (own1)
-                for (int c = tid; c < b; c += kLuThreads)
-                    __stcg(&slots->krow[par1][c], P[(k + 1 - r0) * pitch + c]);
+            lu_publish(slots, par ^ 1, P, pitch, b, r0, r1, k + 1, kc + 1, mine);
             lu_grid_arrive(sync, G, arrivals);
             done_a = mine;
             done_b = own1 ? k + 1 : LLONG_MAX;
