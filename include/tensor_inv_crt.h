@@ -14,11 +14,11 @@
  *     _PRECISION_BITS: 53 float64, 24 float32, 11 float16, 8 bfloat16).
  *
  * Reference interfaces replaced (paths inside the reference project):
- *   ti_n_moduli               src/tensor_inv/crt_matmul.py:26      _n_moduli(k, bits)
- *   ti_crt_split              src/tensor_inv/crt_matmul.py:38,47   _scale_to_int + _residues
+ *   ti_n_moduli               src/tensor_inv/crt_matmul.py:20      _n_moduli(k, bits)
+ *   ti_crt_split              src/tensor_inv/crt_matmul.py:32,41   _scale_to_int + _residues
  *   ti_batched_int8_gemm_mod  src/tensor_inv/csrc/crt_kernel.cu:17 batched_int8_gemm_mod
  *   ti_crt_reconstruct        src/tensor_inv/csrc/crt_kernel.cu:127 crt_reconstruct
- *   ti_crt_matmul             src/tensor_inv/crt_matmul.py:101     crt_matmul (CUDA branch)
+ *   ti_crt_matmul             src/tensor_inv/crt_matmul.py:95     crt_matmul (CUDA branch)
  */
 #ifndef TENSOR_INV_CRT_H
 #define TENSOR_INV_CRT_H
@@ -54,7 +54,7 @@ const char *ti_status_string(int status);
 /* Library version, e.g. "0.1.0". */
 const char *ti_version(void);
 
-/* Replaces crt_matmul.py:26 _n_moduli: smallest N with prod(first N odd primes) >
+/* Replaces crt_matmul.py:20 _n_moduli: smallest N with prod(first N odd primes) >
    2*k*2^(2*bits).  Writes N to *n_out; TI_ERR_UNSUPPORTED if no N <= 30 works. */
 int ti_n_moduli(int64_t k, int bits, int *n_out);
 
@@ -65,7 +65,7 @@ const int32_t *ti_primes(void);
 int ti_crt_workspace_size(int64_t m, int64_t n, int64_t k, int bits, size_t *bytes);
 
 /*
- * Replaces crt_matmul.py:38 _scale_to_int + crt_matmul.py:47 _residues for one operand.
+ * Replaces crt_matmul.py:32 _scale_to_int + crt_matmul.py:41 _residues for one operand.
  * The operand is `outer` vectors of length `kdim` (rows of A, or columns of B); element
  * (o, l) is X[o*s_outer + l*s_k] (device, float64).
  *   exp_out[o]   (device int32[outer]) = frexp(max(max_l |x|, 1e-300)).exponent,
@@ -97,7 +97,7 @@ int ti_batched_int8_gemm_mod(const int8_t *a, const int8_t *b, const int32_t *mo
  * kernel's double-double approximation): x = sum_i r_i M_i (M_i^-1 mod p_i) mod M, lifted
  * to (-M/2, M/2], then out = ldexp((double)x, row_exp[r] + col_exp[c] - 2*bits) with the
  * rounding of Python's float(int) followed by math.ldexp.  Bit-identical to the
- * reference's CPU path (crt_matmul.py:79-98).
+ * reference's CPU path (crt_matmul.py:73-92).
  * residues: device int32 (n_mod, rows, cols); moduli: HOST int32[n_mod], pairwise coprime,
  * each in [2, 256), product below 2^127; row_exp/col_exp: device int32; out: device
  * float64 rows x cols with leading dimension ldo.
@@ -117,7 +117,7 @@ int ti_crt_reconstruct(const int32_t *residues, const int32_t *moduli, int n_mod
  * ranks * 127) passed to ti_crt_reconstruct with the same exponents and moduli gives the
  * crt_matmul of the whole product bit for bit.  A: m x k (this rank's k), B: k x n, strides
  * in elements with one of each pair 1.  No counterpart in the reference, which runs on one
- * device; it splits crt_matmul.py:101-126 at _matmul_residues.
+ * device; it splits crt_matmul.py:95-120 at _matmul_residues.
  * workspace: ti_crt_residue_partial_workspace_size() bytes, 256-byte aligned.
  */
 int ti_crt_residue_partial_workspace_size(int64_t m, int64_t n, int64_t k, int n_mod,
@@ -176,7 +176,7 @@ int ti_crt_workspace_size_ex(int64_t m, int64_t n, int64_t k, int bits,
 #define TI_OUT_ADD 2      /* C += A @ B  */
 
 /*
- * Replaces crt_matmul.py:101 crt_matmul for float64 operands on the device:
+ * Replaces crt_matmul.py:95 crt_matmul for float64 operands on the device:
  *   A (m x k): element (i, l) at A[i*sa0 + l*sa1];  B (k x n): (l, j) at B[l*sb0 + j*sb1];
  *   C (m x n) row-major with leading dimension ldc.
  * Output bits equal the reference CPU path for finite inputs.  Stages: split A and B into
@@ -192,7 +192,7 @@ int ti_crt_matmul(const double *A, int64_t sa0, int64_t sa1, const double *B, in
 /*
  * ti_crt_matmul with options (moduli set, moduli count, profiling events).  With the
  * defaults it is ti_crt_matmul.  No counterpart in the reference, which has no options:
- * it extends crt_matmul.py:101 with an opt-in moduli set and moduli count.
+ * it extends crt_matmul.py:95 with an opt-in moduli set and moduli count.
  */
 int ti_crt_matmul_ex(const double *A, int64_t sa0, int64_t sa1, const double *B, int64_t sb0,
                      int64_t sb1, double *C, int64_t ldc, int64_t m, int64_t n, int64_t k,
@@ -200,7 +200,7 @@ int ti_crt_matmul_ex(const double *A, int64_t sa0, int64_t sa1, const double *B,
                      void *stream, const ti_crt_options_t *opt);
 
 /*
- * crt_matmul on HOST operands (the reference's CPU-tensor call, crt_matmul.py:101), with
+ * crt_matmul on HOST operands (the reference's CPU-tensor call, crt_matmul.py:95), with
  * the copies pipelined against the kernels: all of B goes to the device first, then A in
  * row bands; each band is split, multiplied and reconstructed on `stream` as soon as it has
  * arrived, and its rows of C are copied back while the next band computes.  The three copy
@@ -240,13 +240,28 @@ int ti_crt_matmul_events(const double *A, int64_t sa0, int64_t sa1, const double
  * cudaFree or allocating library routine; its scratch is a static device array of
  * TI_NOALLOC_SCRATCH_BYTES per device, held by every GPU that loads it until the process
  * exits.  Problems whose ti_crt_workspace_size() exceeds that return TI_ERR_SCRATCH_LIMIT
- * (about m = n = k = 940 at float64).  The first call on each device looks up the array's
- * device address and should come before any stream capture.  All calls on a device share
- * the array: calls that overlap on the GPU race and must be serialised by the caller.
+ * (about m = n = k = 940 at float64).  The first call on each device with a non-empty
+ * output looks up the array's device address and should come before any stream capture.
+ * All calls on a device share the array: calls that overlap on the GPU race and must be
+ * serialised by the caller.  It always runs the reference's primes on the default path (no
+ * ti_crt_options_t: no wide moduli, no fixed moduli count); with the tuning switch
+ * TI_CRT_PATH=fused set in the environment every call returns TI_ERR_SCRATCH_LIMIT, because
+ * that kernel's scratch holds one slot per SM.
  */
 int ti_crt_matmul_noalloc(const double *A, int64_t sa0, int64_t sa1, const double *B,
                           int64_t sb0, int64_t sb1, double *C, int64_t ldc, int64_t m, int64_t n,
                           int64_t k, int bits, int out_mode, void *stream);
+
+/*
+ * Self-test of the kernels' bounded waits, for tests: launches a wait that nothing completes
+ * (which = 0: an mbarrier of a one-CTA pipeline whose producer never arrives; which = 1: the
+ * LU panel's grid barrier, waited on for one CTA more than arrive) with a limit of limit_ns
+ * (1e3..1e10) instead of the kernels' 2 s, synchronises `stream` and returns
+ * TI_ERR_DEVICE_TIMEOUT when the wait ran out and recorded its code in the device error word
+ * (left set; read and clear it with ti_device_error).  No counterpart in the reference, whose
+ * kernels have no bounded waits.
+ */
+int ti_selftest_bounded_wait(int which, long long limit_ns, void *stream);
 
 /*
  * Reads (and, if reset != 0, clears) the current device's kernel error word.  Kernels set

@@ -7,12 +7,12 @@ Each wrapper restates one function of the reference module
 ``src/tensor_inv/crt_matmul.py`` on numpy arrays:
 
 =====================  ==============================================
-``n_moduli``           ``_n_moduli``            crt_matmul.py:26-35
+``n_moduli``           ``_n_moduli``            crt_matmul.py:20-29
 ``split``              ``_scale_to_int`` +
-                       ``_residues``            crt_matmul.py:38-52
-``residue_gemm``       ``_matmul_residues``     crt_matmul.py:55-65
-``crt_reconstruct``    ``_crt_reconstruct``     crt_matmul.py:68-98
-``crt_matmul``         ``crt_matmul``           crt_matmul.py:101-126
+                       ``_residues``            crt_matmul.py:32-46
+``residue_gemm``       ``_matmul_residues``     crt_matmul.py:49-59
+``crt_reconstruct``    ``_crt_reconstruct``     crt_matmul.py:62-92
+``crt_matmul``         ``crt_matmul``           crt_matmul.py:95-120
 ``crt_matmul_moduli``  the same with explicit moduli and precision
 =====================  ==============================================
 """
@@ -165,4 +165,61 @@ def crt_matmul_moduli(A: np.ndarray, B: np.ndarray, moduli, bits: int) -> np.nda
                                     _ptr(mods), len(mods), bits, _ptr(out), n)
     if rc != 0:
         raise ValueError(f"oracle failed ({rc})")
+    return out
+
+
+# ---------------------------------------------------------------------------------------
+# The exactly rounded product (the accuracy reference; not part of the reference's path)
+# ---------------------------------------------------------------------------------------
+_SPLIT = 134217729.0  # 2^27 + 1: Veltkamp's splitter for binary64
+
+
+def _two_product(a: np.ndarray, b: np.ndarray):
+    """p + e == a * b exactly, elementwise (Dekker's product with Veltkamp's split), valid while
+    nothing overflows or underflows: |a|, |b| < 2^995 and every partial product, down to
+    2^-106 |a b|, above the normal range's floor (callers check |a b| >= 2^-900)."""
+    c = _SPLIT * a
+    ah = c - (c - a)
+    al = a - ah
+    c = _SPLIT * b
+    bh = c - (c - b)
+    bl = b - bh
+    p = a * b
+    e = ((ah * bh - p) + ah * bl + al * bh) + al * bl
+    return p, e
+
+
+def exact_rounded_matmul(A: np.ndarray, B: np.ndarray) -> np.ndarray:
+    """float64 C[i, j] = the exact sum_k A[i, k] * B[k, j], rounded once to nearest-even.
+
+    Every product is split exactly into two doubles (p + e), and math.fsum returns the
+    correctly rounded sum of its (exact) inputs, so the result is the rounding of the exact
+    rational dot product.  Entries whose products leave the range where the split is exact
+    fall back to exact rational arithmetic (fractions.Fraction).  For the sizes of a sample
+    (a few thousand entries at k = 8192) this takes seconds."""
+    import math
+    from fractions import Fraction
+
+    A = np.ascontiguousarray(A, np.float64)
+    B = np.ascontiguousarray(B, np.float64)
+    m, k = A.shape
+    k2, n = B.shape
+    assert k == k2
+    out = np.empty((m, n), np.float64)
+    Bt = np.ascontiguousarray(B.T)
+    for i in range(m):
+        a = A[i]
+        for j in range(n):
+            b = Bt[j]
+            prod = a * b
+            mag = np.abs(prod)
+            safe = (np.all(np.isfinite(prod)) and np.abs(a).max(initial=0.0) < 2.0**995
+                    and np.abs(b).max(initial=0.0) < 2.0**995
+                    and not np.any((mag > 0) & (mag < 2.0**-900)))
+            if safe:
+                p, e = _two_product(a, b)
+                out[i, j] = math.fsum(np.concatenate([p, e]).tolist())
+            else:
+                out[i, j] = float(sum(Fraction(x) * Fraction(y) for x, y in
+                                      zip(a.tolist(), b.tolist())))
     return out

@@ -8,11 +8,11 @@
  * Every function restates one step of the reference algorithm with plain
  * exact CPU arithmetic (multi-word integers, libm frexp/ldexp/nearbyint):
  *
- *   or_n_moduli          src/tensor_inv/crt_matmul.py:26-35   (_n_moduli)
- *   or_split             src/tensor_inv/crt_matmul.py:38-52   (_scale_to_int + _residues)
- *   or_residue_gemm      src/tensor_inv/crt_matmul.py:55-65   (_matmul_residues, CPU branch)
- *   or_crt_reconstruct   src/tensor_inv/crt_matmul.py:68-98   (_crt_precompute + _crt_reconstruct)
- *   or_crt_matmul        src/tensor_inv/crt_matmul.py:101-126 (crt_matmul, CPU branch)
+ *   or_n_moduli          src/tensor_inv/crt_matmul.py:20-29   (_n_moduli)
+ *   or_split             src/tensor_inv/crt_matmul.py:32-46   (_scale_to_int + _residues)
+ *   or_residue_gemm      src/tensor_inv/crt_matmul.py:49-59   (_matmul_residues, CPU branch)
+ *   or_crt_reconstruct   src/tensor_inv/crt_matmul.py:62-92   (_crt_precompute + _crt_reconstruct)
+ *   or_crt_matmul        src/tensor_inv/crt_matmul.py:95-120 (crt_matmul, CPU branch)
  *   or_crt_matmul_moduli the same path with a caller-chosen moduli set and precision
  *                        (the opt-in wide-moduli scheme; the steps are unchanged)
  *
@@ -156,7 +156,7 @@ static double bn_to_double(const bn_t *a) {
 }
 
 /* ------------------------------------------------------------------------ */
-/* crt_matmul.py:26-35  _n_moduli(k, bits)                                   */
+/* crt_matmul.py:20-29  _n_moduli(k, bits)                                   */
 /* smallest N with prod(first N primes) > 2*k*2^(2*bits); -1 if none         */
 /* ------------------------------------------------------------------------ */
 int or_n_moduli(int64_t k, int bits) {
@@ -175,7 +175,7 @@ int or_n_moduli(int64_t k, int bits) {
 const int *or_primes(void) { return OR_PRIMES; }
 
 /* ------------------------------------------------------------------------ */
-/* crt_matmul.py:38-52  _scale_to_int + _residues for ONE operand.           */
+/* crt_matmul.py:32-46  _scale_to_int + _residues for ONE operand.           */
 /* The operand is viewed as `outer` vectors of length `kdim` (rows of A, or  */
 /* columns of B); element (o, l) lives at X[o*s_outer + l*s_k].              */
 /*   exp_out[o]            = frexp(max(max_l |x|, 1e-300)).exponent          */
@@ -216,7 +216,7 @@ void or_split(const double *X, int64_t outer, int64_t kdim, int64_t s_outer, int
 }
 
 /* ------------------------------------------------------------------------ */
-/* crt_matmul.py:55-65  _matmul_residues (CPU branch):                       */
+/* crt_matmul.py:49-59  _matmul_residues (CPU branch):                       */
 /*   c[i] = (a_res[i].int() @ b_res[i].int()) % moduli[i]                    */
 /* a_res: [n_mod][m][k], b_res: [n_mod][k][n] (the reference layout),       */
 /* c: [n_mod][m][n] int32.  Accumulation is int32, as in torch's int matmul; */
@@ -247,7 +247,7 @@ or_residue_gemm(const int8_t *a_res, const int8_t *b_res, int n_mod, const int32
 }
 
 /* ------------------------------------------------------------------------ */
-/* crt_matmul.py:68-98  _crt_precompute + _crt_reconstruct                  */
+/* crt_matmul.py:62-92  _crt_precompute + _crt_reconstruct                  */
 /*   x = sum_i r_i * M_i * (M_i^-1 mod m_i)  mod M;  x > M//2 -> x - M        */
 /*   out = ldexp(float(x), row_exp + col_exp - 2*bits)                        */
 /* residues: [n_mod][rows][cols] int32; out: rows x cols, leading dim ldo.   */
@@ -320,7 +320,7 @@ int or_crt_reconstruct(const int32_t *residues, int n_mod, const int32_t *moduli
 }
 
 /* ------------------------------------------------------------------------ */
-/* crt_matmul.py:101-126 with an explicit moduli set and precision: the     */
+/* crt_matmul.py:95-120 with an explicit moduli set and precision: the     */
 /* same four steps (scale + residues, per-modulus int32 GEMM mod m_i,       */
 /* bigint CRT, ldexp) for any pairwise-coprime moduli < 256.  bits is used  */
 /* exactly as the reference uses _PRECISION_BITS[dtype].                    */
@@ -375,7 +375,7 @@ done:
 }
 
 /* ------------------------------------------------------------------------ */
-/* crt_matmul.py:101-126  crt_matmul, CPU branch, for float64 operands.     */
+/* crt_matmul.py:95-120  crt_matmul, CPU branch, for float64 operands.     */
 /* A element (i,l) at A[i*sa0 + l*sa1]; B element (l,j) at B[l*sb0 + j*sb1]. */
 /* bits: 53 fp64, 24 fp32, 11 fp16, 8 bf16 (_PRECISION_BITS).                */
 /* Returns 0, -1 when no modulus count covers k, -2 on allocation failure.   */

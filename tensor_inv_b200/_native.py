@@ -70,6 +70,7 @@ SIGNATURES = {
     "ti_crt_matmul_host": (_int, [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i64, _i64,
                                   _int, _p, _sz, _p, _opt]),
     "ti_device_error": (_int, [ctypes.POINTER(_int), _int]),
+    "ti_selftest_bounded_wait": (_int, [_int, ctypes.c_longlong, _p]),
     "ti_crt_residue_partial_workspace_size": (_int, [_i64, _i64, _i64, _int,
                                                      ctypes.POINTER(_sz)]),
     "ti_crt_residue_partial": (_int, [_p, _i64, _i64, _p, _i64, _i64, _i64, _i64, _i64, _int,
@@ -169,6 +170,11 @@ def crt_plan(k: int, bits: int, moduli=None, n_moduli=None):
         if k > limit:
             raise ValueError(f"inner dim {k} exceeds {limit}, the bound that keeps the int32 "
                              f"residue accumulators exact for moduli {moduli or 'primes'!r}")
+        most = 16 if moduli == "wide" else 25
+        if n_moduli is not None and n_moduli > most:
+            raise ValueError(f"n_moduli {n_moduli} exceeds the {most} moduli of the "
+                             f"{moduli or 'primes'!r} set that the reconstruction takes (the "
+                             f"product of the moduli must stay below 2^128)")
         raise ValueError(f"no moduli plan for inner dim {k}, bits {bits}, moduli {moduli!r}, "
                          f"n_moduli {n_moduli!r}")
     check("ti_crt_plan", st)

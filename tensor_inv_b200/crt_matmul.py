@@ -8,11 +8,11 @@ same errors.  Every stage runs in ``libtensor_inv_crt.so``:
 ========================  =====================================  ==========================
 reference                 here                                   C ABI
 ========================  =====================================  ==========================
-crt_matmul.py:26-35       ``_n_moduli``                          ``ti_n_moduli``
-crt_matmul.py:38-52       ``_split`` (scale + residues, fused)   ``ti_crt_split``
-crt_matmul.py:55-65       ``_matmul_residues``                   ``ti_batched_int8_gemm_mod``
-crt_matmul.py:79-98       ``_crt_reconstruct``                   ``ti_crt_reconstruct``
-crt_matmul.py:101-126     ``crt_matmul``                         ``ti_crt_matmul``
+crt_matmul.py:20-29       ``_n_moduli``                          ``ti_n_moduli``
+crt_matmul.py:32-46       ``_split`` (scale + residues, fused)   ``ti_crt_split``
+crt_matmul.py:49-59       ``_matmul_residues``                   ``ti_batched_int8_gemm_mod``
+crt_matmul.py:73-92       ``_crt_reconstruct``                   ``ti_crt_reconstruct``
+crt_matmul.py:95-120     ``crt_matmul``                         ``ti_crt_matmul``
 ========================  =====================================  ==========================
 
 Results are bit-identical to the reference's CPU path for finite inputs.  CPU tensors are
@@ -28,7 +28,7 @@ import torch
 
 from . import _native as nat
 
-# crt_matmul.py:11-15 -- the moduli: the 30 odd primes below 128
+# crt_matmul.py:5-9 -- the moduli: the 30 odd primes below 128
 # fmt: off
 _PRIMES = [
     3, 5, 7, 11, 13, 17, 19, 23, 29, 31, 37, 41, 43, 47, 53,
@@ -36,7 +36,7 @@ _PRIMES = [
 ]
 # fmt: on
 
-# crt_matmul.py:18-23 -- significand bits kept per input dtype
+# crt_matmul.py:12-17 -- significand bits kept per input dtype
 _PRECISION_BITS = {
     torch.float16: 11,
     torch.bfloat16: 8,
@@ -46,7 +46,7 @@ _PRECISION_BITS = {
 
 
 def _n_moduli(k, bits):
-    """min primes whose product covers dot-product range (crt_matmul.py:26-35)"""
+    """min primes whose product covers dot-product range (crt_matmul.py:20-29)"""
     return nat.n_moduli(int(k), int(bits))
 
 
@@ -128,7 +128,7 @@ def _options(k, bits, moduli, n_moduli):
 def crt_matmul(A, B, *, moduli=None, n_moduli=None):
     """FP-accurate matmul via int8 CRT. Precision matches input dtype.
 
-    Same contract as the reference (crt_matmul.py:101-126): ``bits`` from ``A.dtype``,
+    Same contract as the reference (crt_matmul.py:95-120): ``bits`` from ``A.dtype``,
     operands promoted to float64, result float64 on ``A``'s device.
 
     Keyword-only extensions (absent from the reference; the defaults are its scheme):
@@ -281,7 +281,7 @@ def crt_matmul_update(C, A, B, alpha=-1, *, moduli=None, n_moduli=None, lower=Fa
 def _split(X, bits, n_mod, axis_k):
     """Exponents and int8 residues of one float64 CUDA operand.
 
-    Fuses the reference's ``_scale_to_int`` and ``_residues`` (crt_matmul.py:38-52).
+    Fuses the reference's ``_scale_to_int`` and ``_residues`` (crt_matmul.py:32-46).
     ``axis_k`` is the reduction axis (1 for A, 0 for B).  Returns ``(exp int32[outer],
     res int8[n_mod, outer, k])``, the residues of the rows of A or of the columns of B.
     """
@@ -307,7 +307,7 @@ def _split(X, bits, n_mod, axis_k):
 
 
 def _scale_to_int_exponents(A, B, bits):
-    """The exponents of the reference's ``_scale_to_int`` (crt_matmul.py:38-44)."""
+    """The exponents of the reference's ``_scale_to_int`` (crt_matmul.py:32-38)."""
     n_mod = 1
     re, _ = _split(A, bits, n_mod, axis_k=1)
     ce, _ = _split(B, bits, n_mod, axis_k=0)
@@ -315,7 +315,7 @@ def _scale_to_int_exponents(A, B, bits):
 
 
 def _matmul_residues(a_res, b_res, moduli):
-    """per-prime int8 matmul + modular reduction (crt_matmul.py:55-65), on tcgen05.
+    """per-prime int8 matmul + modular reduction (crt_matmul.py:49-59), on tcgen05.
 
     a_res (N, m, k) and b_res (N, k, n) int8 CUDA tensors; returns a list of N int32
     (m, n) tensors with values in [0, p).
@@ -338,7 +338,7 @@ def _matmul_residues(a_res, b_res, moduli):
 
 
 def _crt_reconstruct(residues, moduli, bits, row_exp, col_exp):
-    """Exact CRT reconstruction (crt_matmul.py:79-98) of N int32 (rows, cols) residues."""
+    """Exact CRT reconstruction (crt_matmul.py:73-92) of N int32 (rows, cols) residues."""
     res = torch.stack(list(residues)).to(torch.int32).contiguous()
     N, rows, cols = res.shape
     dev = res.device

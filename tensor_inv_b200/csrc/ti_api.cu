@@ -1,6 +1,6 @@
 // ti_api.cu -- the extern "C" entry points of libtensor_inv_crt.so (include/tensor_inv_crt.h).
 //
-// Host-side planning for the CRT matmul: the modulus count (crt_matmul.py:26 _n_moduli),
+// Host-side planning for the CRT matmul: the modulus count (crt_matmul.py:20 _n_moduli),
 // the per-modulus constants every kernel receives by value, the workspace layout, and the
 // stage sequence K1 (split) -> K2 (tcgen05 residue GEMM) -> K3 (exact CRT).
 #include <cstdlib>
@@ -159,7 +159,7 @@ static int make_plan(int64_t k, int bits, const ti_crt_options_t *opt, Plan &P) 
     if (k > (P.wide ? kMaxKWide : int64_t(TI_MAX_K))) return TI_ERR_UNSUPPORTED;
     if (want > max_n) return TI_ERR_UNSUPPORTED;
     if (want == 0 && !P.wide) {
-        P.n_mod = n_moduli_exact(k, bits);  // crt_matmul.py:26-35
+        P.n_mod = n_moduli_exact(k, bits);  // crt_matmul.py:20-29
         P.bits = bits;
         if (P.n_mod < 0 || P.n_mod > max_n) return TI_ERR_UNSUPPORTED;
     } else if (want == 0) {

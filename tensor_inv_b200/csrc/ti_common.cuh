@@ -152,16 +152,17 @@ __device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity
 }
 
 // Waits for the phase of `bar` with the given parity to complete.  Returns false when the
-// wait exceeds kWaitTimeoutNs or when another role of the CTA raised *abort.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
-                                          volatile int *abort) {
+// wait exceeds limit_ns (kWaitTimeoutNs in every kernel; shorter only in the self-test that
+// makes a wait run out) or when another role of the CTA raised *abort.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort,
+                                          unsigned long long limit_ns = kWaitTimeoutNs) {
     const uint32_t a = smem_u32(bar);
     if (mbar_try_wait(a, parity)) return true;
     const unsigned long long t0 = globaltimer_ns();
     while (true) {
         if (mbar_try_wait_hint(a, parity, 20000u)) return true;
         if (*abort) return false;
-        if (globaltimer_ns() - t0 > kWaitTimeoutNs) return false;
+        if (globaltimer_ns() - t0 > limit_ns) return false;
     }
 }
 

@@ -1,6 +1,6 @@
 // ti_crt.cu -- K3: exact CRT reconstruction + inverse power-of-two scaling to float64.
 //
-// Restates src/tensor_inv/crt_matmul.py:68-98 (_crt_precompute, _crt_reconstruct) exactly:
+// Restates src/tensor_inv/crt_matmul.py:62-92 (_crt_precompute, _crt_reconstruct) exactly:
 //   x   = sum_i r_i * M_i * (M_i^-1 mod p_i)  mod M,   lifted to (-M/2, M/2]
 //   out = math.ldexp(float(x), row_exp + col_exp - 2*bits)
 // and so replaces the reference's double-double approximation (crt_kernel.cu:93-125).

@@ -4,9 +4,9 @@
 // Given, for one element, the four 64-bit column sums of S = sum_i t_i * M_i (t_i =
 // (r_i * u_i) mod p_i, M_i = M / p_i) and the 32.32 fixed-point F = sum_i t_i / p_i, it
 // forms x = S - floor(F + 1/2) * M mod 2^128 (exact), lifts x into [-(M-1)/2, (M-1)/2] as
-// the reference's `x > M // 2 -> x - M` does (crt_matmul.py:93-95), rounds float(x) to
+// the reference's `x > M // 2 -> x - M` does (crt_matmul.py:87-89), rounds float(x) to
 // nearest-even and applies ldexp(., row_exp + col_exp - 2*bits) with gradual underflow
-// (crt_matmul.py:96).
+// (crt_matmul.py:90).
 #pragma once
 
 #include "ti_common.cuh"

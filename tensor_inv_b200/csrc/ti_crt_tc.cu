@@ -1,7 +1,7 @@
 // ti_crt_tc.cu -- K3 with the CRT sums on the tensor cores.
 //
 // Same result, bit for bit, as crt_kernel (ti_crt.cu) on uint8 t-planes; restates
-// src/tensor_inv/crt_matmul.py:68-98 (_crt_precompute, _crt_reconstruct).  For one output
+// src/tensor_inv/crt_matmul.py:62-92 (_crt_precompute, _crt_reconstruct).  For one output
 // element with t_i = (r_i * u_i) mod p_i (i < n_mod, written by the residue GEMM's epilogue):
 //   S = sum_i t_i * M_i  (mod 2^128),     F = sum_i t_i * f_i,   f_i = round(2^48 / p_i),
 // then x = S - floor(F / 2^48 + 1/2) * M and the float64 rounding (crt_finish).

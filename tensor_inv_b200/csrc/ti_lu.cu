@@ -20,6 +20,7 @@
 // caller's workspace; every wait is bounded in time, and on timeout the kernel records an
 // error and all CTAs return.  All accesses to W bypass L1 (ld/st .cg), so
 // a CTA never reads a stale copy of a row that another CTA swapped or updated.
+#include <atomic>
 #include <cstring>
 
 #include "tensor_inv_crt.h"
@@ -126,9 +127,10 @@ __device__ __forceinline__ void lu_grid_arrive(LuSync *s, unsigned nblocks, unsi
     target += nblocks;
 }
 
-// lu_grid_wait: until the count of arrivals reaches `target` (bounded; false in every thread if
-// the wait ran out or another CTA gave up).  Ends with a CTA barrier.
-__device__ bool lu_grid_wait(LuSync *s, unsigned target, int *err) {
+// lu_grid_wait: until the count of arrivals reaches `target` (bounded by limit_ns; false in
+// every thread if the wait ran out or another CTA gave up).  Ends with a CTA barrier.
+__device__ bool lu_grid_wait(LuSync *s, unsigned target, int *err,
+                             unsigned long long limit_ns = kWaitTimeoutNs) {
     __shared__ int ok_sh;
     if (threadIdx.x == 0) {
         int ok = 1;
@@ -138,7 +140,7 @@ __device__ bool lu_grid_wait(LuSync *s, unsigned target, int *err) {
                 ok = 0;
                 break;
             }
-            if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+            if (globaltimer_ns() - t0 > limit_ns) {
                 atomicExch(&s->abort, 1);
                 atomicCAS(err, 0, kErrTimeoutGridBarrier);
                 ok = 0;
@@ -640,9 +642,47 @@ size_t lu_smem_bytes(int64_t rows_per_cta, int64_t b) {
     return size_t(rows_per_cta) * size_t(b + 1) * sizeof(double);
 }
 
+// ---------------------------------------------------------------------------------------
+// Self-test of the bounded waits (ti_selftest_bounded_wait): waits that nothing will ever
+// complete, with a short limit, so the path by which a broken pipeline becomes an error code
+// instead of a hung GPU actually runs.  Both use the library's own wait primitives.
+// ---------------------------------------------------------------------------------------
+
+// One CTA: an mbarrier that expects one arrival which never comes (the wait of an MMA or
+// epilogue warp whose producer died).
+__global__ void __launch_bounds__(32) selftest_mbar_timeout_kernel(unsigned long long limit_ns,
+                                                                   int *err) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+        abort_flag = 0;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && !mbar_wait(&bar, 0, &abort_flag, limit_ns))
+        atomicCAS(err, 0, kErrTimeoutMma);
+}
+
+// `ctas` CTAs: each arrives once at the LU panel's grid barrier and waits for one arrival more
+// than there are CTAs (a CTA that never arrives).
+__global__ void __launch_bounds__(32) selftest_grid_timeout_kernel(LuSync *sync,
+                                                                   unsigned long long limit_ns,
+                                                                   int *err) {
+    unsigned target = 0;
+    lu_grid_arrive(sync, gridDim.x, target);
+    lu_grid_wait(sync, target + 1, err, limit_ns);
+}
+
+__device__ LuSync g_selftest_sync;
+
 }  // namespace ti
 
 using namespace ti;
+
+// Largest dynamic shared memory of lu_panel_smem_kernel on each device (0: not yet set up).
+constexpr int kLuMaxDevices = 64;
+static std::atomic<size_t> g_lu_max_dyn[kLuMaxDevices];
 
 extern "C" {
 
@@ -703,11 +743,13 @@ int ti_lu_panel_ex(double *W, int64_t ldw, int64_t n, int64_t ncols, int64_t j, 
     const size_t smem = lu_smem_bytes(per, b);
     // the largest dynamic shared memory a CTA may take: the opt-in limit less the kernel's
     // static arrays (at b = 256 this holds 111 rows per CTA: n = 16384 on 148 SMs)
-    static int configured = -1;
-    static size_t max_dyn = 0;
+    // (kept per device, set up once on each; threads racing on the first call of a device
+    // both set the same attribute, which is harmless)
     int dev = 0;
-    cudaGetDevice(&dev);
-    if (configured != dev) {
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kLuMaxDevices)
+        return TI_ERR_NO_DEVICE;
+    size_t max_dyn = g_lu_max_dyn[dev].load(std::memory_order_acquire);
+    if (max_dyn == 0) {
         cudaFuncAttributes fa;
         int optin = 0;
         if (cudaFuncGetAttributes(&fa, lu_panel_smem_kernel) != cudaSuccess ||
@@ -719,7 +761,7 @@ int ti_lu_panel_ex(double *W, int64_t ldw, int64_t n, int64_t ncols, int64_t j, 
         if (cudaFuncSetAttribute(lu_panel_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(max_dyn)) != cudaSuccess)
             return TI_ERR_CUDA;
-        configured = dev;
+        g_lu_max_dyn[dev].store(max_dyn, std::memory_order_release);
     }
     if (b <= kLuSmemMaxPanel && smem <= max_dyn) {
         int per_sm_s = 0;
@@ -742,6 +784,33 @@ int ti_lu_panel_ex(double *W, int64_t ldw, int64_t n, int64_t ncols, int64_t j, 
                                     s) != cudaSuccess)
         return TI_ERR_CUDA;
     return TI_OK;
+}
+
+// Test entry: see tensor_inv_crt.h.  Synchronous; the waits run out after limit_ns.
+int ti_selftest_bounded_wait(int which, long long limit_ns, void *stream) {
+    if ((which != 0 && which != 1) || limit_ns < 1000 || limit_ns > 10000000000ll)
+        return TI_ERR_INVALID_ARGUMENT;
+    int num_sms = 0;
+    int *err = nullptr;
+    int rc = device_context(&num_sms, &err);
+    if (rc != TI_OK) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const unsigned long long lim = static_cast<unsigned long long>(limit_ns);
+    if (which == 0) {
+        selftest_mbar_timeout_kernel<<<1, 32, 0, s>>>(lim, err);
+    } else {
+        LuSync *sync = nullptr;
+        if (cudaGetSymbolAddress(reinterpret_cast<void **>(&sync), g_selftest_sync) != cudaSuccess ||
+            cudaMemsetAsync(sync, 0, sizeof(LuSync), s) != cudaSuccess)
+            return TI_ERR_CUDA;
+        selftest_grid_timeout_kernel<<<4, 32, 0, s>>>(sync, lim, err);
+    }
+    if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(s) != cudaSuccess)
+        return TI_ERR_CUDA;
+    int code = 0;
+    if (cudaMemcpy(&code, err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+        return TI_ERR_CUDA;
+    return code != 0 ? TI_ERR_DEVICE_TIMEOUT : TI_OK;
 }
 
 }  // extern "C"

@@ -18,6 +18,12 @@
 // call reads was written earlier by the same call.  Calls whose kernels overlap on the
 // GPU (different streams, or host threads) race on the array and must be serialised by
 // the caller.
+//
+// It always runs the reference's 25-prime scheme through the default single-band path: it
+// takes no ti_crt_options_t, so the wide moduli, a fixed moduli count and the stage events
+// are not available here.  The opt-in fused GEMM+CRT kernel (TI_CRT_PATH=fused in the
+// environment, a tuning switch) sizes its scratch for one slot per SM, about 150-300 MB, so
+// with that switch set every call here returns TI_ERR_SCRATCH_LIMIT.
 #include <atomic>
 
 #include "tensor_inv_crt.h"
@@ -55,6 +61,11 @@ extern "C" int ti_crt_matmul_noalloc(const double *A, int64_t sa0, int64_t sa1, 
     int rc = ti_crt_workspace_size(m, n, k, bits, &need);
     if (rc != TI_OK) return rc;
     if (need > kNoallocScratchBytes) return TI_ERR_SCRATCH_LIMIT;
+    // An empty output needs no scratch: the shapes are checked and nothing is launched, so an
+    // empty call never looks the array up (and may come first, even inside a capture).
+    if (m == 0 || n == 0)
+        return ti_crt_matmul(A, sa0, sa1, B, sb0, sb1, C, ldc, m, n, k, bits, out_mode, nullptr,
+                             0, stream);
     void *scratch = nullptr;
     rc = scratch_for_current_device(&scratch);
     if (rc != TI_OK) return rc;

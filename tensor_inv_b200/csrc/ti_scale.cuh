@@ -1,7 +1,7 @@
 // ti_scale.cuh -- the reference's power-of-two scaling of one float64, in exact integer
 // arithmetic, shared by the split kernels (ti_split.cu, ti_split_tc.cu).
 //
-// Restates src/tensor_inv/crt_matmul.py:38-44 (_scale_to_int): per vector the frexp exponent
+// Restates src/tensor_inv/crt_matmul.py:32-38 (_scale_to_int): per vector the frexp exponent
 // e of max(max |x|, 1e-300), then v = round_half_even(x * 2^(bits - e)) for every element.
 #pragma once
 

@@ -1,6 +1,6 @@
 // ti_split.cu -- K1: fused power-of-two scaling + int8 residue split of one operand.
 //
-// Restates src/tensor_inv/crt_matmul.py:38-52 (_scale_to_int, _residues) in exact integer
+// Restates src/tensor_inv/crt_matmul.py:32-46 (_scale_to_int, _residues) in exact integer
 // arithmetic.  An operand is `outer` vectors of length `kdim` (rows of A or columns of B)
 // with element (o, l) at X[o*s_outer + l*s_k].  Two passes:
 //   1. exponent: e_o = frexp(max(max_l |x_ol|, 1e-300)).exponent (or kNonfiniteExp)

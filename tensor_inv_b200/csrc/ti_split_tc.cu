@@ -1,7 +1,7 @@
 // ti_split_tc.cu -- K1 with the residue arithmetic on the tensor cores.
 //
 // Same residues, bit for bit, as split_rows_kernel / split_cols_kernel with symmetric
-// residues (ti_split.cu); restates src/tensor_inv/crt_matmul.py:38-52 (_scale_to_int,
+// residues (ti_split.cu); restates src/tensor_inv/crt_matmul.py:32-46 (_scale_to_int,
 // _residues) with the representative of each residue in [-(p-1)/2, (p-1)/2].
 //
 // Per element the scaled integer v = round_half_even(x * 2^(bits - e)), |v| <= 2^53, is

@@ -1,7 +1,7 @@
 """Sharding of the CRT matmul and of rSVD over ranks (one process per GPU, torch.distributed).
 
 The product shards with no exchange step: row exponents depend only on A's rows and column
-exponents only on B's columns (src/tensor_inv/crt_matmul.py:38-44), so the output block
+exponents only on B's columns (src/tensor_inv/crt_matmul.py:32-38), so the output block
 C[rows_i, cols_j] of a pr x pc rank grid is exactly ``crt_matmul(A[rows_i], B[:, cols_j])``,
 bit for bit, computed from the rank's own A row panel and B column panel.
 
@@ -130,7 +130,7 @@ _NONFINITE_EXP = -(2**31)
 
 def _global_exponents(X, dim, group):
     """frexp exponents of max |X| along `dim` over every rank's slice (the reference's
-    ``amax().clamp(min=1e-300).frexp()[1]``, crt_matmul.py:38-44), with the non-finite marker.
+    ``amax().clamp(min=1e-300).frexp()[1]``, crt_matmul.py:32-38), with the non-finite marker.
     The maxima are all-reduced as int64 bit patterns: for non-negative float64 the integer
     order is the float order, and NaN's pattern lies above inf's, so the max is exact."""
     import torch.distributed as dist
@@ -163,8 +163,6 @@ def crt_matmul_sharded_k(A_local, B_local, *, group=None):
     from tensor_inv_b200.crt_matmul import _PRIMES, _check_dtype, _n_moduli, _strides_2d
 
     bits = _check_dtype(A_local)
-    if not A_local.is_cuda:
-        raise RuntimeError("crt_matmul_sharded_k needs CUDA tensors")
     dev = A_local.device
     m, kl = A_local.shape
     if B_local.shape[0] != kl:
@@ -175,7 +173,15 @@ def crt_matmul_sharded_k(A_local, B_local, *, group=None):
     k = int(kt.item())
     if k == 0:
         raise IndexError("crt_matmul_sharded_k: empty inner dimension")
+    # every rank sees the same total, so every rank raises together: the whole product's
+    # inner dimension has the single-GPU bound (the sum of the ranks' planes would stay exact
+    # beyond it, but crt_matmul of the whole product raises there, and so does this)
+    if k > nat.TI_MAX_K:
+        raise ValueError(f"inner dim {k} exceeds {nat.TI_MAX_K}, the bound that keeps the int32 "
+                         f"residue accumulators exact for moduli 'primes'")
     n_mod = _n_moduli(k, bits)
+    if not A_local.is_cuda:
+        raise RuntimeError("crt_matmul_sharded_k needs CUDA tensors")
     A = A_local.to(torch.float64)
     B = B_local.to(torch.float64)
     row_exp = _global_exponents(A, 1, group)

@@ -17,7 +17,8 @@ def _mm(X, Y):
 
 def rsvd(A, rank, n_oversamples=10, n_power_iter=1):
     """
-    Randomized SVD via CRT int8 GEMM (Halko-Martinsson-Tropp).
+    Rank-``rank`` SVD of A from a random range finder (Halko, Martinsson and Tropp) whose
+    products all run on the CRT-emulated float64 GEMM.
 
     Returns U (m x rank), S (rank,), Vt (rank x n).
     """

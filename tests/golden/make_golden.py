@@ -1,8 +1,9 @@
 """Generate golden fixtures from the reference implementation itself.
 
-Run in a container where the reference package is importable, e.g.::
+Run where the reference package is importable, with the reference's ``src`` directory on
+the path::
 
-    PYTHONPATH=/root/reference/src python tests/golden/make_golden.py
+    PYTHONPATH=<the reference's src> python tests/golden/make_golden.py
 
 Each case runs the reference's own CPU path (``tensor_inv.crt_matmul``) stage by stage
 and stores every intermediate in ``tests/golden/<case>.npz``:

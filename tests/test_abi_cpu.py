@@ -119,5 +119,9 @@ def test_moduli_plans(nat):
         mods = nat.crt_plan(8, 53, "wide", N)[2]
         assert all(math.gcd(a, c) == 1 for i, a in enumerate(mods) for c in mods[i + 1:])
         assert math.prod(mods) < 2**127
-    with pytest.raises(ValueError):
+    # counts past a set's size: a clear error (17 and 18 moduli come from the primes)
+    with pytest.raises(ValueError, match="exceeds the 16 moduli"):
         nat.crt_plan(8192, 53, "wide", 17)
+    with pytest.raises(ValueError, match="exceeds the 25 moduli"):
+        nat.crt_plan(8192, 53, "primes", 26)
+    assert [nat.crt_plan(8192, 53, "primes", N)[:2] for N in (17, 18)] == [(17, 30), (18, 33)]

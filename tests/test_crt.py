@@ -1,10 +1,7 @@
-"""The reference's tests/test_crt.py, run against tensor_inv_b200 (needs the GPU path)."""
 import pytest
 import torch
 
-from tensor_inv_b200.crt_matmul import crt_matmul
-
-pytestmark = pytest.mark.gpu
+from tensor_inv.crt_matmul import crt_matmul
 
 
 @pytest.fixture

@@ -434,8 +434,9 @@ def test_wide_moduli_vs_reference_scheme(ti, oracle, m, n, k, phi):
     _assert_bitexact(ti.crt_matmul(A.cuda(), B.cuda(), moduli="wide"), want)
 
 
-@pytest.mark.parametrize("n_mod", [12, 13, 14, 15, 16])
-@pytest.mark.parametrize("moduli", ["wide", "primes"])
+@pytest.mark.parametrize("moduli,n_mod", [(mod, n) for mod in ("wide", "primes")
+                                          for n in (12, 13, 14, 15, 16)]
+                         + [("primes", 17), ("primes", 18)])
 def test_moduli_sweep_vs_oracle(ti, oracle, n_mod, moduli):
     """Moduli-count sweep: N moduli, precision lowered to what N moduli can hold; bit-exact
     against the reference algorithm restated with the same moduli and precision."""

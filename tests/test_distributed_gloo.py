@@ -89,3 +89,50 @@ def test_grid_and_ranges():
         (r0, r1), (c0, c1) = D.my_ranges(1000, 700, r, 8)
         covered[r0:r1, c0:c1] += 1
     assert (covered == 1).all()
+
+
+def _sharded_k_worker(rank, world, port, k_local, out_q):
+    import torch.distributed as dist
+
+    from tensor_inv_b200 import distributed as D
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        A = torch.ones(2, k_local, dtype=torch.float64)
+        B = torch.ones(k_local, 3, dtype=torch.float64)
+        try:
+            D.crt_matmul_sharded_k(A, B)
+            out_q.put((rank, "no error"))
+        except ValueError as e:
+            out_q.put((rank, f"ValueError: {e}"))
+        except Exception as e:  # noqa: BLE001 - reported to the parent
+            out_q.put((rank, f"{type(e).__name__}: {e}"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_k_total_inner_dim_bound():
+    """Each rank's slice (70000) is within the accumulator bound, but the whole inner dimension
+    (140000) is not: every rank raises the single-GPU crt_matmul's ValueError, before any
+    device work."""
+    world, k_local = 2, 70000
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_sharded_k_worker, args=(r, world, port, k_local, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        got = dict(q.get(timeout=120) for _ in range(world))
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+    assert sorted(got) == [0, 1]
+    for msg in got.values():
+        assert msg.startswith("ValueError") and "140000 exceeds 135263" in msg, msg

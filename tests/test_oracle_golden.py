@@ -67,3 +67,25 @@ def test_planted_mistake_is_caught(oracle):
     bad = out.copy()
     bad.view(np.uint64)[3, 4] += 1
     assert not np.array_equal(bad.view(np.uint64), g["out"].view(np.uint64))
+
+
+def test_exact_rounded_matmul_against_fractions(oracle):
+    """The accuracy reference (exactly rounded dot products) against exact rationals, on
+    wide-spread inputs, ties-prone integers, cancellation and the rational fallback."""
+    from fractions import Fraction
+
+    rng = np.random.default_rng(3)
+    cases = []
+    for phi in (0.5, 2.0, 6.0):
+        A = (rng.random((5, 300)) - 0.5) * np.exp(phi * rng.standard_normal((5, 300)))
+        B = (rng.random((300, 4)) - 0.5) * np.exp(phi * rng.standard_normal((300, 4)))
+        cases.append((A, B))
+    A = rng.standard_normal((3, 50))
+    cases.append((np.vstack([A, -A]), np.vstack([A, A]).T))           # exact cancellation
+    cases.append((np.full((2, 3), 2.0**53 + 1.0), np.full((3, 2), 1.0 + 2.0**-52)))
+    cases.append((np.array([[1e-200, 3.0]]), np.array([[1e-200], [1.0]])))  # fallback path
+    for A, B in cases:
+        got = oracle.exact_rounded_matmul(A, B)
+        want = np.array([[float(sum(Fraction(x) * Fraction(y) for x, y in zip(A[i], B[:, j])))
+                          for j in range(B.shape[1])] for i in range(A.shape[0])])
+        assert np.array_equal(got.view(np.uint64), want.view(np.uint64))

@@ -1,10 +1,6 @@
-"""The reference's tests/test_rsvd.py, run against tensor_inv_b200."""
-import pytest
 import torch
 
-from tensor_inv_b200.rsvd import rsvd
-
-pytestmark = pytest.mark.gpu
+from tensor_inv.rsvd import rsvd
 
 
 def test_rsvd_low_rank():
