@@ -277,6 +277,153 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def bind_to_gpu_numa_node(dev):
+    """Restrict this process to the host cores next to its GPU (sysfs local_cpulist of the
+    GPU's PCI function), so that pinned host buffers allocated afterwards are first-touched on
+    the GPU's own NUMA node.  Returns the core count bound to, or None when unavailable."""
+    import torch
+
+    try:
+        pr = torch.cuda.get_device_properties(dev)
+        bus = f"{pr.pci_domain_id:04x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        spec = Path(f"/sys/bus/pci/devices/{bus}/local_cpulist").read_text().strip()
+        cpus = set()
+        for part in spec.split(","):
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+        cpus &= os.sched_getaffinity(0)
+        if not cpus:
+            return None
+        os.sched_setaffinity(0, cpus)
+        return len(cpus)
+    except (AttributeError, OSError, ValueError):
+        return None
+
+
+def strong_scaling(args, torch, dist, dev, rank, world, stream, n_mod_opt, mods, bits_kept):
+    """The fixed 8192^3 product over the ranks' pr x pc grid, with its collectives.
+
+    Inputs are resident and distributed before timing: rank r holds rows [r m/W, (r+1) m/W)
+    of A and one piece of B's columns, stored as rows of B^T (the piece that makes the
+    column-group gather produce its grid column's panel).  Each step: all-gather A's row panel
+    over the grid row and B's column panel over the grid column (NCCL over NVLink), the CRT
+    product of the rank's C block, and an all-gather of the C blocks to every rank (block
+    layout).  Every phase is timed with CUDA events on the rank's stream; the phases and the
+    whole step are reported as the max over ranks, with the slowest rank's kernel stages."""
+    import ctypes
+
+    from tensor_inv_b200 import _native as nat
+    from tensor_inv_b200 import distributed as D
+
+    m = n = k = args.size
+    pr, pc = D.grid_shape(world)
+    gi, gj = rank // pc, rank % pc
+    if m % (world * 128) or n % (world * 128):
+        return None
+    rows_per = m // world
+    cols_per = n // world
+    row_groups = [dist.new_group([i * pc + j for j in range(pc)]) for i in range(pr)]
+    col_groups = [dist.new_group([i * pc + j for i in range(pr)]) for j in range(pc)]
+    rg, cg = row_groups[gi], col_groups[gj]
+    # the global problem, generated shard by shard on the ranks that hold them
+    A_shard = synth((rows_per, k), 5000 + rank, args.phi, dev)
+    Bt_shard = synth((cols_per, k), 6000 + gj * pr + gi, args.phi, dev)
+    bm, bn = m // pr, n // pc
+    A_panel = torch.empty((bm, k), dtype=torch.float64, device=dev)
+    Bt_panel = torch.empty((bn, k), dtype=torch.float64, device=dev)
+    C_blk = torch.empty((bm, bn), dtype=torch.float64, device=dev)
+    C_all = torch.empty((world, bm, bn), dtype=torch.float64, device=dev)
+    bits = 53
+    ws_bytes = nat.crt_workspace_size_ex(bm, bn, k, bits, n_mod_opt)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    L = nat.lib()
+
+    def step(evs):
+        evs[0].record(stream)
+        dist.all_gather_into_tensor(A_panel, A_shard, group=rg)
+        dist.all_gather_into_tensor(Bt_panel, Bt_shard, group=cg)
+        evs[1].record(stream)
+        o = nat.CrtOptions(n_mod_opt.moduli, n_mod_opt.n_moduli)
+        for i in range(4):
+            o.stage_events[i] = evs[2 + i].cuda_event
+        st = L.ti_crt_matmul_ex(A_panel.data_ptr(), k, 1, Bt_panel.data_ptr(), 1, k,
+                                C_blk.data_ptr(), bn, bm, bn, k, bits, 0, ws.data_ptr(),
+                                ws_bytes, stream.cuda_stream, ctypes.byref(o))
+        nat.check("ti_crt_matmul_ex", st)
+        dist.all_gather_into_tensor(C_all, C_blk)
+        evs[6].record(stream)
+
+    def events():
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
+        for e in evs:
+            e.record(stream)
+        return evs
+
+    for _ in range(max(3, args.warmup)):
+        step(events())
+    torch.cuda.synchronize(dev)
+    dist.barrier(device_ids=[dev.index])
+    steps = max(5, args.steps)
+    rec = [events() for _ in range(steps)]
+    torch.cuda.synchronize(dev)
+    dist.barrier(device_ids=[dev.index])
+    torch.cuda.synchronize(dev)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for evs in rec:
+        step(evs)
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    dist.barrier(device_ids=[dev.index])
+
+    def mean(a, b):
+        return statistics.mean(e[a].elapsed_time(e[b]) for e in rec)
+
+    mine = [t0.elapsed_time(t1) / steps, mean(0, 1), mean(1, 5), mean(5, 6), mean(2, 3),
+            mean(3, 4), mean(4, 5)]
+    allv = torch.tensor(mine, dtype=torch.float64, device=dev)
+    gathered = [torch.empty_like(allv) for _ in range(world)]
+    dist.all_gather(gathered, allv)
+    per_rank = [g.tolist() for g in gathered]
+    mx = [max(r[i] for r in per_rank) for i in range(len(mine))]
+    slow = max(range(world), key=lambda r: per_rank[r][2])
+    flops = 2.0 * m * n * k
+    # a bit check of one block of every rank's C against the oracle (untimed)
+    import numpy as np
+
+    from oracle import oracle
+
+    r0, c0 = (bm * 2) // 3, (bn * 3) // 5
+    Ab = A_panel[r0:r0 + 8].cpu().numpy()
+    Bb = Bt_panel[c0:c0 + 8].T.cpu().numpy()
+    want = (oracle.crt_matmul(Ab, Bb, 53) if bits_kept == 53
+            else oracle.crt_matmul_moduli(Ab, Bb, mods, bits_kept))
+    got = C_all[rank, r0:r0 + 8, c0:c0 + 8].cpu().numpy()
+    ok = torch.tensor([int(np.array_equal(got.view("u8"), want.view("u8")))], device=dev)
+    dist.all_reduce(ok)
+    for g in row_groups + col_groups:
+        dist.destroy_process_group(g)
+    return {
+        "problem": f"one {m}x{k} @ {k}x{n} product over a {pr}x{pc} grid ({bm}x{bn} C blocks)",
+        "layout": "A rows and B columns sharded 1-D over the ranks before timing; per step: "
+                  "A row panel all-gathered over the grid row, B column panel over the grid "
+                  "column (NCCL, NVLink), the block's CRT product, C blocks all-gathered to "
+                  "every rank (block layout)",
+        "steps": steps, "ms_per_step": mx[0],
+        "phase_ms_max_over_ranks": {"panel_allgather": mx[1], "compute": mx[2],
+                                    "c_allgather": mx[3]},
+        "compute_only_tflops": flops / (mx[2] * 1e-3) / 1e12,
+        "with_panel_allgather_tflops": flops / ((mx[1] + mx[2]) * 1e-3) / 1e12,
+        "with_all_collectives_tflops": flops / (mx[0] * 1e-3) / 1e12,
+        "slowest_compute_rank": slow,
+        "slowest_rank_stages_ms": {"k1_split": per_rank[slow][4], "k2_gemms": per_rank[slow][5],
+                                   "k3_last_crt": per_rank[slow][6]},
+        "per_rank_compute_ms": [r[2] for r in per_rank],
+        "bitexact_blocks": f"{int(ok.item())}/{world}",
+    }
+
+
 def run_ours(args):
     import torch
 
@@ -290,6 +437,7 @@ def run_ours(args):
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    numa_cores = bind_to_gpu_numa_node(dev) if world > 1 else None
     dist = None
     if world > 1:
         import datetime
@@ -415,6 +563,12 @@ def run_ours(args):
         accuracy = error_summary(got, exact, want, k, float(A.abs().max()), float(B.abs().max()))
         accuracy["sample"] = ("16 x 16 block of rank 0's output, exactly rounded dot products; "
                               "the full phi x moduli sweep is bench.py --workload accuracy")
+
+    # ---- the same product at a fixed size over all ranks, with its collectives
+    strong = None
+    if dist is not None:
+        strong = strong_scaling(args, torch, dist, dev, rank, world, stream, opt_main, mods,
+                                bits_kept)
 
     # ---- e2e: public API on pinned host tensors, copies inside the timed region
     # ---- the reference's 25-prime scheme on the same inputs (context for the headline)
@@ -588,6 +742,7 @@ def run_ours(args):
             "gpu_launches": launches_per_call * args.steps, "stages": stages,
             "spot_check_bitexact": spot_ok,
             "spot_check_ranks_bitexact": f"{ranks_ok}/{world}",
+            "strong_scaling": strong, "host_cores_bound_near_gpu": numa_cores,
             "accuracy": accuracy, "reference_moduli": prim, "context_fp64": dgemm,
         }
         print(json.dumps(line), flush=True)
