@@ -247,6 +247,61 @@ def measure_int8_sustained(torch, dev, size=8192, seconds=3.0):
     return 2.0 * size**3 * n / (ms * 1e-3) / 1e12
 
 
+def reference_gpu_context(args):
+    """The reference's own CUDA branch (its crt_kernel.cu extension, built from the reference's
+    source into oracle/_ref, with its call sequence restated in oracle/ref_gpu.py) on this GPU:
+    the same 8192^3 product with its 25 primes, timed with CUDA events, and its error against
+    the exactly rounded product and against the reference's exact CPU path on a sample."""
+    try:
+        import numpy as np
+        import torch
+
+        from oracle import oracle, ref_gpu
+
+        if not torch.cuda.is_available():
+            return {"unavailable": "no CUDA device"}
+        if ref_gpu.built_path() is None:
+            return {"unavailable": "the reference's crt_kernel extension was not built "
+                                   "(oracle/ref_gpu.py build() needs the reference tree)"}
+        dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+        torch.cuda.set_device(dev)
+        m = n = k = args.size
+        A = synth((m, k), 1000, args.phi, dev)
+        B = synth((k, n), 2000, args.phi, dev)
+        C = ref_gpu.crt_matmul_ref_gpu(A, B)
+        torch.cuda.synchronize(dev)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        reps = 3
+        e0.record()
+        for _ in range(reps):
+            C = ref_gpu.crt_matmul_ref_gpu(A, B)
+        e1.record()
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        r0, c0 = (m * 3) // 5, (n * 2) // 3
+        Ab = A[r0:r0 + 16].cpu().numpy()
+        Bb = B[:, c0:c0 + 16].cpu().numpy()
+        got = C[r0:r0 + 16, c0:c0 + 16].cpu().numpy()
+        exact = oracle.exact_rounded_matmul(Ab, Bb)
+        cpu_path = oracle.crt_matmul(Ab, Bb, 53)
+        summ = error_summary(got, exact, cpu_path, k, float(A.abs().max()), float(B.abs().max()))
+        summ.update({
+            "ms_per_call": ms, "emulated_tflops": 2.0 * m * n * k / (ms * 1e-3) / 1e12,
+            "n_moduli": 25, "calls": reps,
+            "outputs_differing_from_the_reference_cpu_path": int(
+                (got.view("u8") != cpu_path.view("u8")).sum()),
+            "sample": "16 x 16 block; reference_scheme_* here is the reference's exact CPU path",
+            "path": "reference crt_kernel.cu (cuBLASLt batched int8 GEMM + mod_reduce + "
+                    "double-double crt_kernel), torch scaling and residues, built for sm_100a",
+        })
+        del A, B, C
+        torch.cuda.empty_cache()
+        return summ
+    except Exception as e:  # noqa: BLE001 - context only; the line still prints
+        return {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -273,6 +328,7 @@ def run_reference(args):
                          "sample": f"{s}x{k} @ {k}x{s} per step, C restatement of the "
                                    "reference CPU path (oracle/), OpenMP over all host threads"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "reference_gpu_context": reference_gpu_context(args),
     }
     print(json.dumps(line), flush=True)
 
