@@ -356,6 +356,123 @@ def bind_to_gpu_numa_node(dev):
         return None
 
 
+def e2e_one_gpu(args, torch, ti, A, B, stream, barrier, max_over_ranks, flops):
+    """crt_matmul on pinned host tensors, copies inside the timed region (one GPU)."""
+    m, k = A.shape
+    n = B.shape[1]
+    Ah = A.cpu().pin_memory()
+    Bh = B.cpu().pin_memory()
+    # warm-up holds each result while the next call allocates its own, as the timed loop
+    # does, so both pinned output blocks exist before timing starts
+    Ch = None
+    for _ in range(3):
+        Ch = ti.crt_matmul(Ah, Bh, moduli=args.moduli, n_moduli=args.n_moduli)
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    w0 = time.perf_counter()
+    e0.record(stream)
+    for _ in range(args.e2e_steps):
+        Ch = ti.crt_matmul(Ah, Bh, moduli=args.moduli, n_moduli=args.n_moduli)
+    e1.record(stream)
+    barrier()
+    wall_e2e = (time.perf_counter() - w0) / args.e2e_steps
+    ms_e2e = max_over_ranks(e0.elapsed_time(e1) / args.e2e_steps)
+    assert Ch.device.type == "cpu" and Ch.shape == (m, n)
+    # the PCIe floor for context: plain pinned copies of the same bytes
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t2 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    A.copy_(Ah, non_blocking=True)
+    t1.record(stream)
+    Ah.copy_(A, non_blocking=True)
+    t2.record(stream)
+    t2.synchronize()
+    return {"value": flops / (ms_e2e * 1e-3) / 1e12, "unit": UNIT,
+            "h2d_bytes_per_step": Ah.numel() * 8 + Bh.numel() * 8,
+            "d2h_bytes_per_step": Ch.numel() * 8, "ms_per_step": ms_e2e,
+            "wall_ms_per_step": wall_e2e * 1e3,
+            "pcie_h2d_gbs": Ah.numel() * 8 / (t0.elapsed_time(t1) * 1e-3) / 1e9,
+            "pcie_d2h_gbs": Ah.numel() * 8 / (t1.elapsed_time(t2) * 1e-3) / 1e9,
+            "path": "crt_matmul(pinned CPU tensors): B, then row bands of A copied in while "
+                    "earlier bands compute; C bands copied out as they finish"}
+
+
+def e2e_grid(args, torch, dist, A, B, C, stream, barrier, max_over_ranks, flops, world, pr, pc,
+             br, bc, dev):
+    """The weak-scaling problem from host memory on the pr x pc grid: the global A (pr row
+    panels) and B (pc column panels) are split over the ranks' pinned host memory, each byte on
+    exactly one rank; every call (distributed.crt_matmul_grid_host) copies each rank's share in,
+    all-gathers the panels over NVLink, computes the rank's C block band by band and copies it
+    out.  Whole-job bytes: every operand byte in once, every C byte out once."""
+    from tensor_inv_b200 import distributed as D
+
+    m, k = A.shape
+    n = B.shape[1]
+    bands = 8
+    if m % (bands * pc) or k % pr:
+        return None
+    r = m // bands // pc
+    rows_g, cols_g = D.grid_groups()
+    A_slices = torch.stack([A[b * pc * r + bc * r: b * pc * r + (bc + 1) * r]
+                            for b in range(bands)]).cpu().pin_memory()
+    B_slice = B[br * (k // pr):(br + 1) * (k // pr)].cpu().pin_memory()
+    out = torch.empty((m, n), dtype=torch.float64, pin_memory=True)
+
+    def call():
+        D.crt_matmul_grid_host(A_slices, B_slice, row_group=rows_g[br], col_group=cols_g[bc],
+                               out=out, moduli=args.moduli, n_moduli=args.n_moduli)
+
+    for _ in range(3):
+        call()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    w0 = time.perf_counter()
+    e0.record(stream)
+    for _ in range(args.e2e_steps):
+        call()
+    e1.record(stream)
+    barrier()
+    wall_e2e = (time.perf_counter() - w0) / args.e2e_steps
+    ms_e2e = max_over_ranks(e0.elapsed_time(e1) / args.e2e_steps)
+    # the host result against this rank's block of the device-resident run, bit for bit
+    same = torch.tensor([int(torch.equal(out.view(torch.int64), C.cpu().view(torch.int64)))],
+                        device=dev)
+    dist.all_reduce(same)
+    # plain pinned copies of this rank's bytes, all ranks at once (the contended PCIe rates)
+    barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t2 = torch.cuda.Event(enable_timing=True)
+    dA = torch.empty(A_slices.shape, dtype=torch.float64, device=dev)
+    t0.record(stream)
+    dA.copy_(A_slices, non_blocking=True)
+    t1.record(stream)
+    out.copy_(C, non_blocking=True)
+    t2.record(stream)
+    t2.synchronize()
+    barrier()
+    h2d_rank = A_slices.numel() * 8 + B_slice.numel() * 8
+    d2h_rank = out.numel() * 8
+    for g in rows_g + cols_g:
+        dist.destroy_process_group(g)
+    return {"value": world * flops / (ms_e2e * 1e-3) / 1e12, "unit": UNIT,
+            "h2d_bytes_per_step": h2d_rank * world, "d2h_bytes_per_step": d2h_rank * world,
+            "bytes_note": "whole job, all ranks; each operand byte crosses PCIe once",
+            "h2d_bytes_per_rank": h2d_rank, "d2h_bytes_per_rank": d2h_rank,
+            "ms_per_step": ms_e2e, "wall_ms_per_step": wall_e2e * 1e3,
+            "pcie_h2d_gbs_per_rank_contended": A_slices.numel() * 8 / (t0.elapsed_time(t1)
+                                                                       * 1e-3) / 1e9,
+            "pcie_d2h_gbs_per_rank_contended": d2h_rank / (t1.elapsed_time(t2) * 1e-3) / 1e9,
+            "bitexact_vs_device_blocks": f"{int(same.item())}/{world}",
+            "path": "distributed.crt_matmul_grid_host: host shares in, A row panels gathered "
+                    f"over grid rows in {bands} bands and B column panels over grid columns "
+                    "(NCCL, NVLink), each band of C computed and copied out as the next "
+                    "arrives"}
+
+
 def strong_scaling(args, torch, dist, dev, rank, world, stream, n_mod_opt, mods, bits_kept):
     """The fixed 8192^3 product over the ranks' pr x pc grid, with its collectives.
 
@@ -668,45 +785,11 @@ def run_ours(args):
                  "note": "torch.matmul float64 on the same device-resident operands, 3 calls "
                          "after 2 warm-up calls; context only"}
 
-    Ah = A.cpu().pin_memory()
-    Bh = B.cpu().pin_memory()
-    # warm-up holds each result while the next call allocates its own, as the timed loop
-    # does, so both pinned output blocks exist before timing starts
-    Ch = None
-    for _ in range(3):
-        Ch = ti.crt_matmul(Ah, Bh, moduli=args.moduli, n_moduli=args.n_moduli)
-    barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    w0 = time.perf_counter()
-    e0.record(stream)
-    for _ in range(args.e2e_steps):
-        Ch = ti.crt_matmul(Ah, Bh, moduli=args.moduli, n_moduli=args.n_moduli)
-    e1.record(stream)
-    barrier()
-    wall_e2e = (time.perf_counter() - w0) / args.e2e_steps
-    ms_e2e = max_over_ranks(e0.elapsed_time(e1) / args.e2e_steps)
-    assert Ch.device.type == "cpu" and Ch.shape == (m, n)
-    # the PCIe floor for context: plain pinned copies of the same bytes
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    t2 = torch.cuda.Event(enable_timing=True)
-    t0.record(stream)
-    A.copy_(Ah, non_blocking=True)
-    t1.record(stream)
-    Ah.copy_(A, non_blocking=True)
-    t2.record(stream)
-    t2.synchronize()
-    h2d_gbs = Ah.numel() * 8 / (t0.elapsed_time(t1) * 1e-3) / 1e9
-    d2h_gbs = Ah.numel() * 8 / (t1.elapsed_time(t2) * 1e-3) / 1e9
-    e2e = {"value": world * flops / (ms_e2e * 1e-3) / 1e12, "unit": UNIT,
-           "h2d_bytes_per_step": Ah.numel() * 8 + Bh.numel() * 8,
-           "d2h_bytes_per_step": Ch.numel() * 8, "ms_per_step": ms_e2e,
-           "wall_ms_per_step": wall_e2e * 1e3, "pcie_h2d_gbs": h2d_gbs,
-           "pcie_d2h_gbs": d2h_gbs,
-           "path": "crt_matmul(pinned CPU tensors): B, then row bands of A copied in while earlier "
-                   "bands compute; C bands copied out as they finish"}
-    del Ah, Bh, Ch
+    if world == 1:
+        e2e = e2e_one_gpu(args, torch, ti, A, B, stream, barrier, max_over_ranks, flops)
+    else:
+        e2e = e2e_grid(args, torch, dist, A, B, C, stream, barrier, max_over_ranks, flops,
+                       world, pr, pc, br, bc, dev)
 
     # ---- int8 tensor peaks: cuBLAS int8 measured here, and 2x the measured bf16 dense peaks,
     # each as a burst and sustained for seconds under the power cap.

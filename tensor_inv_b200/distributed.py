@@ -122,6 +122,115 @@ def gather_blocks(C_block, m: int, n: int, *, group=None):
     return C
 
 
+def grid_groups(group=None):
+    """(row groups, column groups) of the pr x pc rank grid: ``row[i]`` holds the ranks of grid
+    row i, ``col[j]`` those of grid column j.  Every rank must call this (it creates process
+    groups, in the same order on every rank)."""
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    pr, pc = grid_shape(world)
+    glob = [_global_rank(group, r) for r in range(world)]
+    rows = [dist.new_group([glob[i * pc + j] for j in range(pc)]) for i in range(pr)]
+    cols = [dist.new_group([glob[i * pc + j] for i in range(pr)]) for j in range(pc)]
+    return rows, cols
+
+
+def crt_matmul_grid_host(A_slices, B_slice, *, row_group, col_group, out=None, moduli=None,
+                         n_moduli=None, matmul=None, device=None):
+    """This rank's block C = A_panel @ B_panel of a product whose operands are in host memory,
+    each byte held by exactly one rank of the grid: the ranks of a grid row share its A row
+    panel and those of a grid column its B column panel, so every operand byte crosses PCIe
+    once and reaches the other ranks that need it over NVLink.
+
+    A_slices (bands, r, k): this rank's share of its A row panel, which is cut into `bands`
+    row bands of q*r rows (q the ranks of the grid row); band b of the panel is the rows
+    ``A_slices[b]`` of the row's ranks in group order.  B_slice (k/p, n_b): this rank's rows
+    of its B column panel (p the ranks of the grid column, rows in group order).  Returns the
+    (bands*q*r) x n_b block in host memory (``out`` if given, else pinned).
+
+    On CUDA each band's A rows are copied in and all-gathered over the grid row (NCCL), its
+    block of C is computed (``crt_matmul``, bit-identical to the product of the whole panels:
+    row exponents depend on their row only) and copied out while later bands arrive; the B
+    panel is gathered first (its column exponents need every row).  Synchronous: returns once
+    C is in host memory.  ``matmul`` replaces the product (CPU tests)."""
+    import torch.distributed as dist
+
+    from tensor_inv_b200.crt_matmul import crt_matmul
+
+    bands, r, k = A_slices.shape
+    q = dist.get_world_size(row_group)
+    p = dist.get_world_size(col_group)
+    if B_slice.shape[0] * p != k:
+        raise RuntimeError("crt_matmul_grid_host: B slices do not cover k")
+    n_b = B_slice.shape[1]
+    rows = q * r
+    dev = torch.device(device) if device is not None else (
+        torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available()
+        else torch.device("cpu"))
+    cuda = dev.type == "cuda"
+    if out is None:
+        out = torch.empty((bands * rows, n_b), dtype=torch.float64, pin_memory=cuda)
+
+    def product(a, b_):
+        if matmul is not None:
+            return matmul(a, b_)
+        return crt_matmul(a, b_, moduli=moduli, n_moduli=n_moduli)
+
+    if not cuda:  # gloo ranks on the host: the same data flow, in order
+        B = torch.empty((k, n_b), dtype=torch.float64)
+        dist.all_gather_into_tensor(B, B_slice.to(torch.float64).contiguous(), group=col_group)
+        for b in range(bands):
+            Ab = torch.empty((rows, k), dtype=torch.float64)
+            dist.all_gather_into_tensor(Ab, A_slices[b].to(torch.float64).contiguous(),
+                                        group=row_group)
+            out[b * rows:(b + 1) * rows] = product(Ab, B)
+        return out
+
+    compute = torch.cuda.current_stream(dev)
+    h2d = torch.cuda.Stream(dev)      # PCIe in: B's rows, then the A bands, never waiting
+    gather = torch.cuda.Stream(dev)   # NCCL: B's gather, then the A bands' gathers, in order
+    d2h = torch.cuda.Stream(dev)      # PCIe out: each band of C as soon as it is computed
+    h2d.wait_stream(compute)
+    gather.wait_stream(compute)
+
+    def copied(src):
+        with torch.cuda.stream(h2d):
+            t = src.to(dev, torch.float64, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(h2d)
+        return t, ev
+
+    B_part, ev_b = copied(B_slice)
+    parts = [copied(A_slices[b]) for b in range(bands)]
+    with torch.cuda.stream(gather):
+        B = torch.empty((k, n_b), dtype=torch.float64, device=dev)
+        gather.wait_event(ev_b)
+        # one order of collectives on every rank: B's gather completes before the A bands'
+        dist.all_gather_into_tensor(B, B_part, group=col_group, async_op=True).wait()
+        b_in = torch.cuda.Event()
+        b_in.record(gather)
+        panels, works = [], []
+        for b in range(bands):
+            gather.wait_event(parts[b][1])
+            panels.append(torch.empty((rows, k), dtype=torch.float64, device=dev))
+            works.append(dist.all_gather_into_tensor(panels[b], parts[b][0], group=row_group,
+                                                     async_op=True))
+    compute.wait_event(b_in)  # B is in (the band gathers are waited on one by one)
+    for b in range(bands):
+        works[b].wait()  # the compute stream waits for band b's gather
+        Cb = product(panels[b], B)
+        done = torch.cuda.Event()
+        done.record(compute)
+        d2h.wait_event(done)
+        with torch.cuda.stream(d2h):
+            out[b * rows:(b + 1) * rows].copy_(Cb, non_blocking=True)
+            Cb.record_stream(d2h)
+    d2h.synchronize()
+    # every side-stream buffer is done: h2d -> gather -> compute -> d2h, and d2h has finished
+    return out
+
+
 # ---------------------------------------------------------------------------------------
 # products over a sharded inner dimension, and rSVD with A's rows sharded
 # ---------------------------------------------------------------------------------------
@@ -342,26 +451,61 @@ def _trailing_update(Wv, A, B, k, matmul, lower=False):
         Wv -= crt_matmul(A, B, moduli=caller_moduli(k))
 
 
+def _inverse_perm(piv):
+    """pos with pos[piv[i]] = i: the current position of each original row."""
+    pos = torch.empty_like(piv)
+    pos[piv] = torch.arange(piv.numel(), device=piv.device)
+    return pos
+
+
+def _apply_row_perm_(W, piv, new_piv, j, max_moved):
+    """Reorder W's rows from the order `piv` to `new_piv` (both list the original row at each
+    position), moving only the rows whose position changed: at most `max_moved` (a panel's
+    swaps touch its own rows and the rows they were exchanged with).  No host round trip."""
+    src = _inverse_perm(piv)[new_piv]
+    moved = src != torch.arange(src.numel(), device=src.device)
+    idx = torch.nonzero_static(moved, size=max_moved, fill_value=j).flatten()
+    W[idx] = W[src[idx]]  # the right side is gathered before any row is written
+
+
+def _post_broadcast(tensors, src, group, world):
+    """Asynchronous broadcasts from `src` (none with one rank); returns the works to wait on."""
+    import torch.distributed as dist
+
+    if world == 1:
+        return []
+    return [dist.broadcast(t, src=src, group=group, async_op=True) for t in tensors]
+
+
 def lu_cyclic(W_local, n: int, block_size: int = 64, *, group=None, matmul=None):
-    """Blocked LU with partial pivoting (lu.py:6-54) on block-cyclic columns.
+    """Blocked LU with partial pivoting (lu.py:6-54) on block-cyclic columns, with one step of
+    look-ahead.
 
     W_local holds this rank's block columns of the n x n matrix (``cyclic_columns``), all n
-    rows.  Per block column: its owner factorises the panel (``ti_lu_panel_ex`` on CUDA
-    float64, else the reference's torch loop) with row swaps across its local columns, then
-    broadcasts the pivot vector and the panel; the other ranks apply the same row permutation
-    to their columns.  The U block row is assembled exactly from every rank's columns and
-    solved whole on each rank (the reference's call, so the same bits), and each rank updates
-    its own trailing columns: a column subset of the reference's product, which the CRT
-    kernels compute bit for bit (column exponents depend on their column only).  Returns this
-    rank's factored columns and the pivot vector (the same on every rank)."""
+    rows.  Per block column c: the pivot vector and the panel (factorised by the owner with
+    row swaps across its local columns: ``ti_lu_panel_ex`` on CUDA float64, else the
+    reference's torch loop) are broadcast and the other ranks apply the same row permutation
+    to their columns (only the rows that moved).  The U block row is assembled exactly from
+    every rank's columns and solved whole on each rank (the reference's call, so the same
+    bits).  Look-ahead: the owner of block c + 1 updates that block first, factorises it and
+    posts its broadcast before its remaining update of step c, so the next panel is
+    factorised while the other ranks update; its remaining update then uses L21's rows in the
+    new panel's row order (each entry of W still meets the same row of L21).  Every trailing
+    update is a column subset of the reference's product, which the CRT kernels compute bit
+    for bit (column exponents depend on their column only).  Returns this rank's factored
+    columns and the pivot vector (the same on every rank)."""
     import torch.distributed as dist
 
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     b = block_size
+    nb = -(-n // b)
     W = W_local.clone()
     dev = W.device
     mine = cyclic_blocks(n, b, rank, world)
     local_off = {c: i * b for i, c in enumerate(mine)}
+    # global column of each local column, on the device once (no host copies in the loop,
+    # which would make the host wait for the queued work and end the overlap)
+    gcol = cyclic_columns(n, b, rank, world).to(dev)
     piv = torch.arange(n, device=dev)
     lu_mod = importlib.import_module("tensor_inv_b200.lu")  # the module, not the function
     device_panel = W.is_cuda and W.dtype == torch.float64 and not lu_mod._TORCH_PANEL
@@ -370,49 +514,73 @@ def lu_cyclic(W_local, n: int, block_size: int = 64, *, group=None, matmul=None)
 
         ws = torch.empty(nat.lu_panel_workspace_size(), dtype=torch.uint8, device=dev)
         stream = torch.cuda.current_stream(dev)
-    for j in range(0, n, b):
-        c = j // b
-        bw = min(b, n - j)
+
+    def width(c):
+        return min(b, n - c * b)
+
+    def factor(c):
+        """The owner's panel of block c; returns the broadcast buffers (panel, pivots)."""
+        nonlocal piv
+        j, bw = c * b, width(c)
+        lc = local_off[c]
+        if device_panel and bw <= 1024:
+            nat.lu_panel_cols(W, j, j + bw, lc, piv, ws, stream)
+        else:
+            _panel_torch_cols(W, piv, j, j + bw, lc)
+        return W[j:, lc:lc + bw].contiguous(), piv.clone()
+
+    def post(c, bufs):
+        owner = c % world
+        if bufs is None:  # receivers
+            bufs = (torch.empty((n - c * b, width(c)), dtype=W.dtype, device=dev),
+                    torch.empty_like(piv))
+        return bufs, _post_broadcast([bufs[1], bufs[0]], _global_rank(group, 0 if world == 1
+                                                                       else owner), group, world)
+
+    pending = post(0, factor(0) if rank == 0 else None)
+    for c in range(nb):
+        (panel, new_piv), works = pending
+        for w in works:
+            w.wait()
+        j, bw = c * b, width(c)
         jb = j + bw
         owner = c % world
-        if rank == owner:
-            lc = local_off[c]
-            if device_panel and bw <= 1024:
-                nat.lu_panel_cols(W, j, jb, lc, piv, ws, stream)
-            else:
-                _panel_torch_cols(W, piv, j, jb, lc)
-            panel = W[j:, lc:lc + bw].contiguous()
-            new_piv = piv.clone()
-        else:
-            panel = torch.empty((n - j, bw), dtype=W.dtype, device=dev)
-            new_piv = torch.empty_like(piv)
-        src = _global_rank(group, owner)
-        dist.broadcast(new_piv, src=src, group=group)
-        dist.broadcast(panel, src=src, group=group)
         if rank != owner:
             # the owner's row swaps, as one permutation of rows j.. (piv moved with the rows)
-            pos = torch.empty_like(piv)
-            pos[piv] = torch.arange(n, device=dev)
-            W[j:] = W[pos[new_piv[j:]]]
+            _apply_row_perm_(W, piv, new_piv, j, 2 * bw)
             piv = new_piv
-        if jb < n:
-            L_panel = torch.tril(panel[:bw], diagonal=-1) + torch.eye(bw, dtype=W.dtype,
-                                                                       device=dev)
-            later = [c2 for c2 in mine if c2 > c]
-            row = torch.zeros((bw, n - jb), dtype=W.dtype, device=dev)
-            if later:
-                lo = local_off[later[0]]
-                gcols = torch.cat([torch.arange(c2 * b, min(n, (c2 + 1) * b))
-                                   for c2 in later]).to(dev) - jb
-                row[:, gcols] = W[j:jb, lo:]
+        if jb >= n:
+            break
+        L_panel = torch.tril(panel[:bw], diagonal=-1) + torch.eye(bw, dtype=W.dtype, device=dev)
+        later = [c2 for c2 in mine if c2 > c]
+        row = torch.zeros((bw, n - jb), dtype=W.dtype, device=dev)
+        if later:
+            lo = local_off[later[0]]
+            gcols = gcol[lo:] - jb
+            row[:, gcols] = W[j:jb, lo:]
+        if world > 1:
             _exact_sum_(row, group)
-            # triangular solve for the U block row (lu.py:38-43), whole on every rank
-            U = torch.linalg.solve_triangular(L_panel, row, upper=False)
-            if later:
-                U_mine = U[:, gcols]
-                W[j:jb, lo:] = U_mine
-                # trailing update of this rank's columns (lu.py:46)
-                _trailing_update(W[jb:, lo:], panel[bw:], U_mine, bw, matmul)
+        # triangular solve for the U block row (lu.py:38-43), whole on every rank
+        U = torch.linalg.solve_triangular(L_panel, row, upper=False)
+        L21 = panel[bw:]
+        c1 = c + 1
+        next_bufs = None
+        if later:
+            U_mine = U[:, gcols]
+            W[j:jb, lo:] = U_mine
+            if later[0] == c1:
+                # look-ahead: block c + 1 first (lu.py:46 restricted to its columns), then its
+                # panel, whose broadcast is posted before the rest of this update
+                w1 = width(c1)
+                _trailing_update(W[jb:, lo:lo + w1], L21, U_mine[:, :w1], bw, matmul)
+                pos_before = _inverse_perm(piv)
+                next_bufs = factor(c1)
+                L21 = L21[pos_before[piv[jb:]] - jb]  # L21's rows in the new row order
+                lo, U_mine = lo + w1, U_mine[:, w1:]
+        pending = post(c1, next_bufs)
+        if later and U_mine.shape[1]:
+            # trailing update of this rank's remaining columns (lu.py:46)
+            _trailing_update(W[jb:, lo:], L21, U_mine, bw, matmul)
     return W, piv
 
 
@@ -438,63 +606,101 @@ def lu_distributed(A, block_size: int = 64, *, group=None, matmul=None):
     return P, L, U
 
 
-def cholesky_cyclic(A_local, n: int, block_size: int = 64, *, group=None, matmul=None):
-    """Blocked right-looking Cholesky (cholesky.py:6-35) on block-cyclic columns.
+def _contiguous_runs(blocks, parts):
+    """`blocks` (ascending) cut into at most `parts` runs of consecutive entries."""
+    if not blocks:
+        return []
+    parts = max(1, min(parts, len(blocks)))
+    size = -(-len(blocks) // parts)
+    return [blocks[i:i + size] for i in range(0, len(blocks), size)]
 
-    The owner of a block column computes its diagonal block's Cholesky factor and the panel
-    below it (the reference's calls), broadcasts the panel, and every rank updates its own
-    trailing columns with W[:, cols] -= L21 @ L21[cols]^T (all rows below the panel: the
-    lower-triangle tile skip of one GPU needs whole columns).  The factor's values are the
-    reference's bit for bit.  Returns this rank's columns of L."""
+
+def cholesky_cyclic(A_local, n: int, block_size: int = 64, *, group=None, matmul=None,
+                    update_parts: int = 4):
+    """Blocked right-looking Cholesky (cholesky.py:6-35) on block-cyclic columns, with one step
+    of look-ahead.
+
+    The owner of a block column computes its diagonal block's Cholesky factor
+    (``torch.linalg.cholesky_ex``: the reference's factorisation without a host round trip
+    per block) and the panel below it (the reference's triangular solve), and broadcasts the
+    panel with the block's error code.  Every rank updates its own trailing columns,
+    W[:, cols] -= L21 @ L21[cols]^T, only from each column's diagonal block down (the rows the
+    factorisation reads again), in up to `update_parts` pieces of consecutive local blocks,
+    each from its first block's diagonal down.  Look-ahead: the owner of block c + 1 updates
+    that block first, factorises it and posts its broadcast before the rest of its update
+    of step c.  The factor is the reference's bit for bit; the error codes are checked once
+    at the end, and every rank raises the error the first failing block gives
+    ``torch.linalg.cholesky``.  Returns this rank's columns of L."""
     import torch.distributed as dist
+
+    from tensor_inv_b200.cholesky import _raise_first_failure
 
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     b = block_size
+    nb = -(-n // b)
     W = A_local.clone()
     L = torch.zeros_like(W)
     dev = W.device
     mine = cyclic_blocks(n, b, rank, world)
     local_off = {c: i * b for i, c in enumerate(mine)}
-    for j in range(0, n, b):
-        c = j // b
-        bw = min(b, n - j)
+    gcol = cyclic_columns(n, b, rank, world).to(dev)  # global column of each local column
+    infos = []
+
+    def width(c):
+        return min(b, n - c * b)
+
+    def factor(c):
+        """The owner's diagonal block and panel of block c; returns the broadcast buffers."""
+        j, bw = c * b, width(c)
+        jb, lc = j + bw, local_off[c]
+        # panel: small Cholesky on the diagonal block (cholesky.py:24)
+        Lkk, info = torch.linalg.cholesky_ex(W[j:jb, lc:lc + bw])
+        L[j:jb, lc:lc + bw] = Lkk
+        if jb < n:
+            # triangular solve for the sub-diagonal block (cholesky.py:28-30)
+            L[jb:, lc:lc + bw] = torch.linalg.solve_triangular(
+                Lkk, W[jb:, lc:lc + bw].T, upper=False).T
+        return L[jb:, lc:lc + bw].contiguous(), info.reshape(1).to(torch.int32)
+
+    def post(c, bufs):
+        if bufs is None:  # receivers
+            bufs = (torch.empty((n - c * b - width(c), width(c)), dtype=W.dtype, device=dev),
+                    torch.empty(1, dtype=torch.int32, device=dev))
+        return bufs, _post_broadcast([bufs[1], bufs[0]],
+                                     _global_rank(group, 0 if world == 1 else c % world),
+                                     group, world)
+
+    def update(blocks, L21, jb, bw):
+        """W[:, blocks] -= L21 @ L21[blocks]^T from the first block's diagonal down
+        (cholesky.py:33 restricted to these columns and rows)."""
+        c0 = blocks[0]
+        lo = local_off[c0]
+        hi = local_off[blocks[-1]] + width(blocks[-1])
+        r0 = c0 * b
+        _trailing_update(W[r0:, lo:hi], L21[r0 - jb:], L21[gcol[lo:hi] - jb].T, bw, matmul)
+
+    pending = post(0, factor(0) if rank == 0 else None)
+    for c in range(nb):
+        (L21, info), works = pending
+        for w in works:
+            w.wait()
+        infos.append(info)
+        j, bw = c * b, width(c)
         jb = j + bw
-        owner = c % world
-        failure = None
-        if rank == owner:
-            lc = local_off[c]
-            try:
-                # panel: small Cholesky on the diagonal block (cholesky.py:24)
-                L[j:jb, lc:lc + bw] = torch.linalg.cholesky(W[j:jb, lc:lc + bw])
-                if jb < n:
-                    # triangular solve for the sub-diagonal block (cholesky.py:28-30)
-                    L[jb:, lc:lc + bw] = torch.linalg.solve_triangular(
-                        L[j:jb, lc:lc + bw], W[jb:, lc:lc + bw].T, upper=False
-                    ).T
-            except RuntimeError as e:  # not positive definite: every rank must learn of it
-                failure = e
-        if world > 1:
-            flag = torch.tensor([1 if failure is not None else 0], device=dev)
-            dist.broadcast(flag, src=_global_rank(group, owner), group=group)
-            if int(flag.item()) and failure is None:
-                raise RuntimeError(f"cholesky_distributed: the panel at column {j} failed on "
-                                   f"rank {owner} (matrix not positive definite?)")
-        if failure is not None:
-            raise failure
         if jb >= n:
             break
-        if rank == owner:
-            L21 = L[jb:, lc:lc + bw].contiguous()
-        else:
-            L21 = torch.empty((n - jb, bw), dtype=W.dtype, device=dev)
-        dist.broadcast(L21, src=_global_rank(group, owner), group=group)
         later = [c2 for c2 in mine if c2 > c]
-        if later:
-            lo = local_off[later[0]]
-            gcols = torch.cat([torch.arange(c2 * b, min(n, (c2 + 1) * b))
-                               for c2 in later]).to(dev) - jb
-            # trailing update of this rank's columns (cholesky.py:33)
-            _trailing_update(W[jb:, lo:], L21, L21[gcols].T, bw, matmul)
+        c1 = c + 1
+        next_bufs = None
+        if later and later[0] == c1:
+            # look-ahead: block c + 1 first, then its panel, broadcast before the rest
+            update([c1], L21, jb, bw)
+            next_bufs = factor(c1)
+            later = later[1:]
+        pending = post(c1, next_bufs)
+        for run in _contiguous_runs(later, update_parts):
+            update(run, L21, jb, bw)
+    _raise_first_failure(torch.cat(infos).cpu())
     return L
 
 

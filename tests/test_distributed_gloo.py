@@ -136,3 +136,59 @@ def test_sharded_k_total_inner_dim_bound():
     assert sorted(got) == [0, 1]
     for msg in got.values():
         assert msg.startswith("ValueError") and "140000 exceeds 135263" in msg, msg
+
+
+def _grid_host_worker(rank, world, port, bands, out_q):
+    import torch.distributed as dist
+
+    from oracle import oracle
+    from tensor_inv_b200 import distributed as D
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        pr, pc = D.grid_shape(world)
+        i, j = D.grid_coords(rank, world)
+        rows_g, cols_g = D.grid_groups()
+        mb, nb, k = 96, 70, 60          # one rank's C block, the inner dimension
+        g = torch.Generator().manual_seed(9)
+        A = torch.randn(pr * mb, k, generator=g, dtype=torch.float64)  # the whole operands,
+        B = torch.randn(k, pc * nb, generator=g, dtype=torch.float64)  # rebuilt on every rank
+        Ap = A[i * mb:(i + 1) * mb]                      # this rank's A row panel
+        Bp = B[:, j * nb:(j + 1) * nb]                   # and B column panel
+        r = mb // bands // pc
+        A_slices = torch.stack([Ap[b * pc * r + j * r: b * pc * r + (j + 1) * r]
+                                for b in range(bands)])
+        B_slice = Bp[i * (k // pr):(i + 1) * (k // pr)]
+        C = D.crt_matmul_grid_host(A_slices, B_slice, row_group=rows_g[i], col_group=cols_g[j],
+                                   matmul=lambda a, b: torch.from_numpy(
+                                       oracle.crt_matmul(a.numpy(), b.numpy(), 53)),
+                                   device="cpu")
+        want = oracle.crt_matmul(Ap.numpy(), Bp.numpy(), 53)
+        out_q.put((rank, bool(np.array_equal(C.numpy().view(np.uint64), want.view(np.uint64)))))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,bands", [(2, 4), (4, 2)])
+def test_grid_host_product_matches_the_blocks(oracle, world, bands):
+    """Host-resident operands, each byte on one rank: every rank's C block, assembled from band
+    gathers over its grid row and a B gather over its grid column, equals the oracle's product
+    of the rank's panels bit for bit."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_grid_host_worker, args=(r, world, port, bands, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        got = dict(q.get(timeout=120) for _ in range(world))
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+    assert got == {r: True for r in range(world)}, got
