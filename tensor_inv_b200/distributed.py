@@ -122,14 +122,17 @@ def gather_blocks(C_block, m: int, n: int, *, group=None):
     return C
 
 
-def grid_groups(group=None):
-    """(row groups, column groups) of the pr x pc rank grid: ``row[i]`` holds the ranks of grid
-    row i, ``col[j]`` those of grid column j.  Every rank must call this (it creates process
-    groups, in the same order on every rank)."""
+def grid_groups(group=None, shape=None):
+    """(row groups, column groups) of the pr x pc rank grid (``shape``, default
+    ``grid_shape``): ``row[i]`` holds the ranks of grid row i, ``col[j]`` those of grid column
+    j, rank r at (r // pc, r % pc).  Every rank must call this (it creates process groups, in
+    the same order on every rank)."""
     import torch.distributed as dist
 
     world = dist.get_world_size(group)
-    pr, pc = grid_shape(world)
+    pr, pc = shape if shape is not None else grid_shape(world)
+    if pr * pc != world:
+        raise ValueError(f"grid {pr}x{pc} does not hold {world} ranks")
     glob = [_global_rank(group, r) for r in range(world)]
     rows = [dist.new_group([glob[i * pc + j] for j in range(pc)]) for i in range(pr)]
     cols = [dist.new_group([glob[i * pc + j] for i in range(pr)]) for j in range(pc)]
