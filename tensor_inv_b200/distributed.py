@@ -488,9 +488,10 @@ def lu_cyclic(W_local, n: int, block_size: int = 64, *, group=None, matmul=None)
     rows.  Per block column c: the pivot vector and the panel (factorised by the owner with
     row swaps across its local columns: ``ti_lu_panel_ex`` on CUDA float64, else the
     reference's torch loop) are broadcast and the other ranks apply the same row permutation
-    to their columns (only the rows that moved).  The U block row is assembled exactly from
-    every rank's columns and solved whole on each rank (the reference's call, so the same
-    bits).  Look-ahead: the owner of block c + 1 updates that block first, factorises it and
+    to their columns (only the rows that moved).  Each rank solves the U block row at its full
+    width with the other ranks' columns zero (the reference's call on the same shape; a
+    column's solution depends only on that column and L, so its own columns carry the
+    whole-row solve's bits, and no exchange is needed).  Look-ahead: the owner of block c + 1 updates that block first, factorises it and
     posts its broadcast before its remaining update of step c, so the next panel is
     factorised while the other ranks update; its remaining update then uses L21's rows in the
     new panel's row order (each entry of W still meets the same row of L21).  Every trailing
@@ -561,9 +562,10 @@ def lu_cyclic(W_local, n: int, block_size: int = 64, *, group=None, matmul=None)
             lo = local_off[later[0]]
             gcols = gcol[lo:] - jb
             row[:, gcols] = W[j:jb, lo:]
-        if world > 1:
-            _exact_sum_(row, group)
-        # triangular solve for the U block row (lu.py:38-43), whole on every rank
+        # triangular solve for the U block row (lu.py:38-43): the reference's call on the whole
+        # block row's shape, with the other ranks' columns zero.  Each column of the solution
+        # depends only on its own column and L (the same call on the same shape), so this
+        # rank's columns carry the bits of the whole-row solve, with no exchange
         U = torch.linalg.solve_triangular(L_panel, row, upper=False)
         L21 = panel[bw:]
         c1 = c + 1

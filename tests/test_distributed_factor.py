@@ -118,10 +118,11 @@ def _gpu_worker(rank, world, port, kind, n, block):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("kind,n,block", [("randn", 700, 64), ("ties", 300, 64),
-                                          ("spd", 650, 64), ("randn", 1300, 256)])
-def test_cyclic_factorizations_gpu_match_one_gpu(kind, n, block):
-    mp.spawn(_gpu_worker, args=(2, _free_port(), kind, n, block), nprocs=2, join=True)
+@pytest.mark.parametrize("kind,n,block,world", [("randn", 700, 64, 2), ("ties", 300, 64, 2),
+                                                ("spd", 650, 64, 2), ("randn", 1300, 256, 2),
+                                                ("randn", 1100, 128, 3), ("spd", 1500, 128, 3)])
+def test_cyclic_factorizations_gpu_match_one_gpu(kind, n, block, world):
+    mp.spawn(_gpu_worker, args=(world, _free_port(), kind, n, block), nprocs=world, join=True)
 
 
 def _cpu_fail_worker(rank, world, port, errs):
