@@ -41,10 +41,10 @@ METRIC = "emulated FP64 GEMM TFLOP/s at 8192³, 1/2/4/8 B200; % of int8 TC peak"
 UNIT = "TFLOP/s"
 GRIDS = {1: (1, 1), 2: (1, 2), 4: (2, 2), 8: (2, 4)}
 # dram__bytes_read.sum + dram__bytes_write.sum of one residue-GEMM launch (the CTA-pair kernel)
-# at 8192^3 with the 16 wide moduli, and only there: the mean of three launches (5.12 GB read +
-# 1.06 GB written) from a 1-pass ncu launch list of this bench at 8192^3 (another box gave
-# 6.59 + 1.06 GB: the re-reads of B depend on how the pairs drift apart).
-GEMM_DRAM_BYTES_8192 = 6186950229
+# at 8192^3 with the 16 wide moduli, and only there: one captured launch (7.01 GB read + 1.06 GB
+# written; other boxes gave 5.0-6.6 GB of reads: the re-reads of B depend on how the pairs
+# drift apart).
+GEMM_DRAM_BYTES_8192 = 8073134848
 # A timed region shorter than this runs at the burst clocks: its rates are compared with the
 # burst peak; longer ones with the sustained (power-capped) peak.
 SUSTAINED_AFTER_S = 1.0
