@@ -125,6 +125,8 @@ def cpu_sample_run(k, s, phi, seed=7):
 
     from oracle import oracle
 
+    oracle.set_threads(cpu_threads())  # every host thread, whatever the launcher's OMP setting
+
     A = synth((s, k), seed, phi, "cpu").numpy()
     B = synth((k, s), seed + 1, phi, "cpu").numpy()
     t0 = time.perf_counter()

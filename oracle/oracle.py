@@ -147,7 +147,13 @@ def crt_matmul(A: np.ndarray, B: np.ndarray, bits: int = 53) -> np.ndarray:
 
 
 def set_threads(n: int) -> None:
+    """Threads of the oracle's parallel loops, whatever OMP_NUM_THREADS says (a launcher such
+    as torchrun sets it to 1 for every process)."""
     os.environ["OMP_NUM_THREADS"] = str(n)
+    L = lib()
+    L.or_set_threads.argtypes = [ctypes.c_int]
+    L.or_set_threads.restype = None
+    L.or_set_threads(int(n))
 
 
 def crt_matmul_moduli(A: np.ndarray, B: np.ndarray, moduli, bits: int) -> np.ndarray:

@@ -31,6 +31,9 @@
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
 
 #define OR_NONFINITE_EXP (-2147483647 - 1)
 #define OR_MAX_MODULI 30
@@ -159,6 +162,15 @@ static double bn_to_double(const bn_t *a) {
 /* crt_matmul.py:20-29  _n_moduli(k, bits)                                   */
 /* smallest N with prod(first N primes) > 2*k*2^(2*bits); -1 if none         */
 /* ------------------------------------------------------------------------ */
+/* Threads of the oracle's parallel loops (OpenMP); overrides OMP_NUM_THREADS. */
+void or_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
 int or_n_moduli(int64_t k, int bits) {
     if (k < 0 || bits < 0 || 2 * bits + 1 + 64 > 32 * BN_WORDS - 8) return -1;
     bn_t target, prod;
