@@ -29,6 +29,7 @@
 //
 // Every wait is bounded; on timeout the CTA raises an error word, drains its in-flight
 // copies and MMAs, frees TMEM and exits.
+#include <atomic>
 #include <cstdlib>
 #include <cstring>
 
@@ -528,14 +529,19 @@ bool make_plane_map(CUtensorMap *map, const void *base, int64_t kdim, int64_t ro
     return r == CUDA_SUCCESS;
 }
 
+// Sets the kernel's dynamic shared-memory limit once per device (kept per device, so calls on
+// several devices from several host threads each set up their own; threads racing on the
+// first call of a device both set the same attribute, which is harmless).
 template <bool kFused>
 static cudaError_t configure(int dev) {
-    static int configured = -1;  // last device configured
-    if (configured == dev) return cudaSuccess;
+    constexpr int kMaxDev = 64;
+    static std::atomic<int> configured[kMaxDev];
+    if (dev < 0 || dev >= kMaxDev) return cudaErrorInvalidDevice;
+    if (configured[dev].load(std::memory_order_acquire)) return cudaSuccess;
     cudaError_t e = cudaFuncSetAttribute(residue_gemm_kernel<kFused>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(kGemmSmemBytes));
-    if (e == cudaSuccess) configured = dev;
+    if (e == cudaSuccess) configured[dev].store(1, std::memory_order_release);
     return e;
 }
 
