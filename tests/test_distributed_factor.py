@@ -157,3 +157,32 @@ def test_cyclic_cholesky_failure_reaches_every_rank():
         p.join(timeout=120)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     assert errs.empty(), errs.get()
+
+
+def test_row_permutation_moves_only_changed_rows():
+    """The non-owners' row swaps: applying the owner's pivot vector by moving only the rows
+    whose position changed equals the full permutation gather."""
+    from tensor_inv_b200 import distributed as D
+
+    g = torch.Generator().manual_seed(3)
+    n, j, b = 40, 8, 6
+    W = torch.randn(n, 5, generator=g, dtype=torch.float64)
+    piv = torch.randperm(n, generator=g)
+    new_piv = piv.clone()
+    for k in range(j, j + b):  # the panel's swaps: row k with some row at or below it
+        p = int(torch.randint(k, n, (1,), generator=g))
+        new_piv[[k, p]] = new_piv[[p, k]]
+    pos = D._inverse_perm(piv)
+    want = W[pos[new_piv]]
+    got = W.clone()
+    D._apply_row_perm_(got, piv, new_piv, j, 2 * b)
+    assert torch.equal(got, want)
+
+
+def test_contiguous_runs():
+    from tensor_inv_b200 import distributed as D
+
+    assert D._contiguous_runs([], 4) == []
+    assert D._contiguous_runs([3, 5, 7], 4) == [[3], [5], [7]]
+    assert D._contiguous_runs(list(range(10)), 4) == [[0, 1, 2], [3, 4, 5], [6, 7, 8], [9]]
+    assert sum(D._contiguous_runs(list(range(10)), 1), []) == list(range(10))
