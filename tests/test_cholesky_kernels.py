@@ -68,12 +68,13 @@ def _reference_loop(A, block_size):
     return L
 
 
-def test_cholesky_matches_reference_loop_bitwise():
+@pytest.mark.parametrize("n", [700, 4096])
+def test_cholesky_matches_reference_loop_bitwise(n):
     """The diagonal blocks through cholesky_ex (no host sync per block) give the reference
-    loop's L bit for bit."""
+    loop's L bit for bit (4096: trailing updates large enough for every tile path)."""
     g = torch.Generator().manual_seed(7)
-    X = torch.randn(700, 700, generator=g, dtype=torch.float64)
-    A = (X @ X.T / 700 + 1e-3 * torch.eye(700, dtype=torch.float64)).cuda()
+    X = torch.randn(n, n, generator=g, dtype=torch.float64)
+    A = (X @ X.T / n + 1e-3 * torch.eye(n, dtype=torch.float64)).cuda()
     got = cholesky(A, block_size=256)
     want = _reference_loop(A, 256)
     assert torch.equal(got.view(torch.int64), want.view(torch.int64))

@@ -54,7 +54,7 @@ def _zero_column(n):
 
 
 @pytest.mark.parametrize("n,block,make", [
-    (128, 32, None), (300, 64, None), (1000, 256, None), (257, 256, None),
+    (128, 32, None), (300, 64, None), (1000, 256, None), (257, 256, None), (4096, 256, None),
     (96, 32, _ties), (200, 64, _zero_column),
 ])
 def test_device_panel_is_bit_identical(monkeypatch, n, block, make):
