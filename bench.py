@@ -726,10 +726,10 @@ def run_ours(args):
     from oracle import oracle
 
     r0, c0 = (m * 3) // 5, (n * 2) // 3
-    Ab = A[r0:r0 + 16].cpu().numpy()
-    Bb = B[:, c0:c0 + 16].cpu().numpy()
+    Ab = A[r0:r0 + 32].cpu().numpy()
+    Bb = B[:, c0:c0 + 32].cpu().numpy()
     want = oracle.crt_matmul(Ab, Bb, 53)
-    got = C[r0:r0 + 16, c0:c0 + 16].cpu().numpy()
+    got = C[r0:r0 + 32, c0:c0 + 32].cpu().numpy()
     if bits_kept == 53:
         spot_ok = bool((got.view("u8") == want.view("u8")).all())
     else:  # a lowered precision is compared with the same scheme restated on the CPU
@@ -744,7 +744,7 @@ def run_ours(args):
     if rank == 0:
         exact = oracle.exact_rounded_matmul(Ab, Bb)
         accuracy = error_summary(got, exact, want, k, float(A.abs().max()), float(B.abs().max()))
-        accuracy["sample"] = ("16 x 16 block of rank 0's output, exactly rounded dot products; "
+        accuracy["sample"] = ("32 x 32 block of rank 0's output, exactly rounded dot products; "
                               "the full phi x moduli sweep is bench.py --workload accuracy")
 
     # ---- the same product at a fixed size over all ranks, with its collectives
